@@ -1,0 +1,17 @@
+"""hipgemm_b200 — a B200-native (sm_100a) FP8 e4m3 TN GEMM with bf16 output.
+
+C ABI: include/hipgemm_b200.h, implemented in csrc/ and built into
+libhipgemm_b200.so (python -m hipgemm_b200.build).  This package binds it for
+callers that hold their buffers in torch tensors, and adds the M-sharded
+multi-GPU driver (shard.py).
+"""
+from ._lib import (HGEMM_ERR_ALIGNMENT, HGEMM_ERR_CUDA, HGEMM_ERR_DEVICE_TIMEOUT, HGEMM_ERR_INVALID_VALUE,
+                   HGEMM_ERR_NO_DEVICE, HGEMM_ERR_UNSUPPORTED, HGEMM_OK, LIB_PATH, HgemmError, check, config_names,
+                   lib)
+from .gemm import device_status, fp8_gemm_tn, fp8_gemm_tn_rows, host_init_random, host_make_quantized
+
+__all__ = [
+    "HGEMM_OK", "HGEMM_ERR_INVALID_VALUE", "HGEMM_ERR_ALIGNMENT", "HGEMM_ERR_UNSUPPORTED", "HGEMM_ERR_CUDA",
+    "HGEMM_ERR_NO_DEVICE", "HGEMM_ERR_DEVICE_TIMEOUT", "LIB_PATH", "HgemmError", "check", "config_names", "lib",
+    "device_status", "fp8_gemm_tn", "fp8_gemm_tn_rows", "host_init_random", "host_make_quantized",
+]

@@ -1,0 +1,113 @@
+"""Torch-facing wrappers of the C ABI (device memory and streams come from torch;
+the arithmetic runs in the sm_100a kernels of libhipgemm_b200.so).
+
+    C = fp8_gemm_tn(A, B, scale_a, scale_b)    # C[M,N] bf16 = sa*sb * A[M,K] . B[N,K]^T
+
+mirrors the reference operator fp8_gemm_4wave_256x256x128<M,N,K>(A, B_T, C)
+(nirw4nna/hipgemm fp8_4wave.hpp:334-338): same operand order and layouts, with the
+per-tensor scales of the benchmark configs added and any M, N % 8, K % 16 accepted.
+"""
+from __future__ import annotations
+
+import ctypes
+
+import torch
+
+from ._lib import HgemmError, check, lib
+
+_FP8_DTYPES = (torch.uint8, torch.float8_e4m3fn)
+
+
+def _ptr(t: torch.Tensor | None) -> int | None:
+    return None if t is None else t.data_ptr()
+
+
+def _stream_handle(stream: torch.cuda.Stream | None) -> int | None:
+    s = stream if stream is not None else torch.cuda.current_stream()
+    return s.cuda_stream or None
+
+
+def _check_operand(name: str, t: torch.Tensor) -> None:
+    if t.dtype not in _FP8_DTYPES:
+        raise TypeError(f"{name} must be float8_e4m3fn or uint8 (e4m3 bits), got {t.dtype}")
+    if t.dim() != 2 or not t.is_contiguous():
+        raise ValueError(f"{name} must be a contiguous 2-D tensor")
+    if not t.is_cuda:
+        raise ValueError(f"{name} must be on a CUDA device (there is no CPU path)")
+
+
+def _check_scale(name: str, s: torch.Tensor | None, device: torch.device) -> None:
+    if s is None:
+        return
+    if s.dtype != torch.float32 or s.numel() != 1 or s.device != device:
+        raise ValueError(f"{name} must be a 1-element float32 tensor on {device}")
+
+
+def fp8_gemm_tn(a: torch.Tensor, b: torch.Tensor, scale_a: torch.Tensor | None = None,
+                scale_b: torch.Tensor | None = None, out: torch.Tensor | None = None, *, config: int = 0,
+                stream: torch.cuda.Stream | None = None) -> torch.Tensor:
+    """C[M,N] (bf16) = scale_a * scale_b * a[M,K] @ b[N,K]^T, fp32 accumulation."""
+    _check_operand("a", a)
+    _check_operand("b", b)
+    M, K = a.shape
+    N, Kb = b.shape
+    if Kb != K:
+        raise ValueError(f"K mismatch: a is {tuple(a.shape)}, b is {tuple(b.shape)}")
+    if b.device != a.device:
+        raise ValueError("a and b must be on the same device")
+    _check_scale("scale_a", scale_a, a.device)
+    _check_scale("scale_b", scale_b, a.device)
+    if out is None:
+        out = torch.empty((M, N), dtype=torch.bfloat16, device=a.device)
+    elif out.dtype != torch.bfloat16 or tuple(out.shape) != (M, N) or not out.is_contiguous():
+        raise ValueError("out must be a contiguous (M, N) bfloat16 tensor")
+    with torch.cuda.device(a.device):
+        rc = lib().hgemm_fp8_tn_config(_ptr(a), _ptr(b), _ptr(out), M, N, K, _ptr(scale_a), _ptr(scale_b),
+                                       _stream_handle(stream), int(config))
+    check(rc, "hgemm_fp8_tn")
+    return out
+
+
+def fp8_gemm_tn_rows(a: torch.Tensor, b: torch.Tensor, out: torch.Tensor, row_begin: int, row_end: int,
+                     scale_a: torch.Tensor | None = None, scale_b: torch.Tensor | None = None,
+                     stream: torch.cuda.Stream | None = None) -> torch.Tensor:
+    """Rows [row_begin, row_end) of fp8_gemm_tn(a, b) written into the same rows of `out`."""
+    _check_operand("a", a)
+    _check_operand("b", b)
+    M, K = a.shape
+    N = b.shape[0]
+    if out.dtype != torch.bfloat16 or tuple(out.shape) != (M, N) or not out.is_contiguous():
+        raise ValueError("out must be a contiguous (M, N) bfloat16 tensor")
+    with torch.cuda.device(a.device):
+        rc = lib().hgemm_fp8_tn_rows(_ptr(a), _ptr(b), _ptr(out), M, N, K, int(row_begin), int(row_end),
+                                     _ptr(scale_a), _ptr(scale_b), _stream_handle(stream))
+    check(rc, "hgemm_fp8_tn_rows")
+    return out
+
+
+def device_status() -> int:
+    """Reads and clears the current device's kernel status word (0 = healthy)."""
+    v = ctypes.c_uint32(0)
+    rc = lib().hgemm_device_status(ctypes.byref(v))
+    if rc not in (0, -6):
+        raise HgemmError(rc, "hgemm_device_status")
+    return int(v.value)
+
+
+# ---- host utilities (utils.hpp mirror) -------------------------------------------------
+
+def host_init_random(n: int, seed: int = 0, mean: float = -1.0, stddev: float = 1.0) -> torch.Tensor:
+    """utils.hpp:27-33: mt19937(seed) -> normal_distribution<float>(mean, stddev) -> e4m3.
+    Returns n e4m3 bytes in a CPU uint8 tensor (defaults are the reference's)."""
+    out = torch.empty(n, dtype=torch.uint8)
+    lib().hgemm_host_init_random(out.data_ptr(), n, seed, mean, stddev)
+    return out
+
+
+def host_make_quantized(n: int, seed: int, mean: float = 0.0, stddev: float = 1.0,
+                        out: torch.Tensor | None = None) -> tuple[torch.Tensor, float]:
+    """Per-tensor amax/448 quantisation of n seeded N(mean, stddev) draws (CPU)."""
+    if out is None:
+        out = torch.empty(n, dtype=torch.uint8)
+    scale = lib().hgemm_host_make_quantized(out.data_ptr(), n, seed, mean, stddev)
+    return out, float(scale)

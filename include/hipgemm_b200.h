@@ -1,0 +1,121 @@
+/*
+ * hipgemm_b200 — FP8 e4m3 TN GEMM for NVIDIA B200 (sm_100a), C ABI.
+ *
+ *   C[M x N] (bf16, row-major) = scale_a * scale_b * A[M x K] . B[N x K]^T
+ *
+ * A and B are OCP e4m3 bytes, row-major with K contiguous (B is the reference's
+ * B_T), accumulation is fp32 in tensor memory, the result is rounded to bf16 with
+ * round-to-nearest-even.  Plain pointers and sizes only: no CUDA or torch types in
+ * the signatures (hgemm_stream_t is the same type as cudaStream_t / CUstream).
+ *
+ * Drop-in boundary.  The reference exposes one __global__ template that the caller
+ * launches itself (nirw4nna/hipgemm fp8_4wave.hpp:334-338, launched at test.cpp:79
+ * and bench.cpp:55,78 with <<<(M*N)/(256*256), 256>>>), unscaled, void-returning,
+ * errors surfaced by hipGetLastError + exit (utils.hpp:7-11).  Here the launch is a
+ * function call that returns a status code; the template wrapper at the end of this
+ * header keeps the reference's name and template shape.
+ *
+ * Threading: every entry point is stream-ordered and asynchronous (except those
+ * marked synchronous), reentrant, and safe to call from several host threads.  The
+ * first call on a device does a one-time set-up under a mutex (SM count, kernel
+ * shared-memory attributes); make that first call before any stream capture.
+ */
+#ifndef HIPGEMM_B200_H
+#define HIPGEMM_B200_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+typedef struct CUstream_st* hgemm_stream_t;
+
+/* Status codes.  Never calls exit(); the reference's CHECK_HIP_ERROR (utils.hpp:7-11)
+ * terminates the process instead. */
+#define HGEMM_OK 0
+#define HGEMM_ERR_INVALID_VALUE (-1)   /* null pointer for a non-empty operand, negative size, bad range */
+#define HGEMM_ERR_ALIGNMENT (-2)       /* K % 16, N % 8, or a pointer not 16-byte aligned (TMA rules) */
+#define HGEMM_ERR_UNSUPPORTED (-3)     /* a size beyond what the kernels address (M, N, K < 2^31) */
+#define HGEMM_ERR_CUDA (-4)            /* a CUDA runtime/driver call failed (launch, tensor map, ...) */
+#define HGEMM_ERR_NO_DEVICE (-5)       /* no CUDA device, or not an sm_100 device */
+#define HGEMM_ERR_DEVICE_TIMEOUT (-6)  /* a bounded wait inside a kernel expired (see hgemm_device_status) */
+
+/* Replaces fp8_gemm_4wave_256x256x128<M,N,K> (fp8_4wave.hpp:334-338) for any shape:
+ *   C = bf16_rne((scale_a * scale_b) * sum_k A[m][k] * B[n][k])
+ * A: M x K e4m3 row-major.  B: N x K e4m3 row-major.  C: M x N bf16 row-major,
+ * write-only (fully overwritten; never read).  d_scale_a / d_scale_b: device pointers
+ * to one fp32 each, or NULL for 1.0 (the reference is unscaled).
+ * Requirements: M, N, K >= 0; K % 16 == 0 and N % 8 == 0 (TMA row strides are
+ * multiples of 16 bytes); A, B, C 16-byte aligned.  M == 0 or N == 0 is a no-op;
+ * K == 0 writes zeros.  Returns HGEMM_OK or a negative HGEMM_ERR_* code. */
+int hgemm_fp8_tn(const void* A, const void* B, void* C, int M, int N, int K, const float* d_scale_a,
+                 const float* d_scale_b, hgemm_stream_t stream);
+
+/* Rows [row_begin, row_end) of the same product, written to rows [row_begin, row_end)
+ * of C: the per-rank call of the M-sharded multi-GPU path (each rank holds all of B).
+ * A and C are the FULL matrices' base pointers.  No counterpart in the reference,
+ * which is single-GPU (its grid always covers all of M, test.cpp:79). */
+int hgemm_fp8_tn_rows(const void* A, const void* B, void* C, int M, int N, int K, int row_begin, int row_end,
+                      const float* d_scale_a, const float* d_scale_b, hgemm_stream_t stream);
+
+/* Same as hgemm_fp8_tn with the tile configuration forced (benchmarks and tests):
+ * config 0 = automatic choice; see hgemm_config_name() for the others. */
+int hgemm_fp8_tn_config(const void* A, const void* B, void* C, int M, int N, int K, const float* d_scale_a,
+                        const float* d_scale_b, hgemm_stream_t stream, int config);
+
+/* Number of tile configurations and their names ("bn256_s4" ...); NULL past the end. */
+int hgemm_num_configs(void);
+const char* hgemm_config_name(int config);
+
+/* Synchronous.  Reads and clears the current device's kernel status word: 0 when no
+ * bounded wait has expired since the last call, else the code of the first one. */
+int hgemm_device_status(uint32_t* status_out);
+
+/* Human-readable text for an HGEMM_* status code (static storage). */
+const char* hgemm_error_string(int code);
+
+/* Library version string. */
+const char* hgemm_version(void);
+
+/* ---- host utilities mirroring the reference harness (utils.hpp) ---------------------- */
+
+/* utils.hpp:27-33 init_random, generalised: std::mt19937(seed) feeding
+ * std::normal_distribution<float>(mean, stddev), each draw converted to e4m3 with
+ * CUDA's host conversion (OCP e4m3, round-to-nearest-even, saturate to finite).
+ * The reference uses mean -1, stddev 1, seed 0. */
+void hgemm_host_init_random(uint8_t* out, size_t n, uint64_t seed, float mean, float stddev);
+
+/* The benchmark configs' per-tensor quantiser: draws n values from N(mean, stddev)
+ * with std::mt19937(seed), scale = amax / 448 (fp32), q[i] = e4m3(x[i] / scale).
+ * Returns the scale (1.0 for an all-zero tensor). */
+float hgemm_host_make_quantized(uint8_t* q, size_t n, uint64_t seed, float mean, float stddev);
+
+/* Quantise caller-provided fp32 values the same way; returns the scale. */
+float hgemm_host_quantize_e4m3(const float* x, size_t n, uint8_t* q);
+
+/* One value through CUDA's host e4m3 / bf16 conversions (for checks). */
+uint8_t hgemm_host_fp8_encode(float x);
+uint16_t hgemm_host_bf16_rne(float x);
+
+#ifdef __cplusplus
+} /* extern "C" */
+
+/* Header-only drop-in for the reference's launcher surface (fp8_4wave.hpp:334-338).
+ * At a call site, `fp8_gemm_4wave_256x256x128<M, N, K><<<grid, 256>>>(A, B_T, C);`
+ * becomes `fp8_gemm_4wave_256x256x128<M, N, K>(A, B_T, C);` (grid and block are
+ * chosen inside), with optional per-tensor scales and a stream.  Unlike the reference
+ * template it accepts any M, N (N % 8 == 0) and K (K % 16 == 0), and returns a
+ * status code instead of requiring hipGetLastError. */
+template <int M, int N, int K>
+inline int fp8_gemm_4wave_256x256x128(const void* A, const void* B_T, void* C, const float* d_scale_a = nullptr,
+                                      const float* d_scale_b = nullptr, hgemm_stream_t stream = nullptr) {
+    static_assert(M >= 0 && N >= 0 && K >= 0, "sizes must be non-negative");
+    static_assert(K % 16 == 0, "K must be a multiple of 16 (TMA row stride)");
+    static_assert(N % 8 == 0, "N must be a multiple of 8 (TMA row stride of C)");
+    return hgemm_fp8_tn(A, B_T, C, M, N, K, d_scale_a, d_scale_b, stream);
+}
+#endif /* __cplusplus */
+
+#endif /* HIPGEMM_B200_H */

@@ -1,0 +1,387 @@
+"""Benchmark of the B200 FP8 e4m3 TN GEMM (C = sa*sb * A . B^T, bf16 out).
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
+                    [--workload 8192|4096|ffn|skinny128|1024x7168x2048|4000x5120x7168|512]
+                    [--allgather] [--config auto|bn256_s4|...]
+
+One step = one GEMM launch over one batch (one rotating (A, B) pair) of the workload;
+at N > 1 (launched by torchrun) rows of M are split across the ranks and B is
+replicated (hipgemm_b200/shard.py), so total work is fixed ("strong" scaling).
+Timing follows the reference's bench.cpp:16-115 (rotating input buffers to defeat the
+cache, warm-up, CUDA events) with the contract's rules: W warm-up steps, exactly K
+timed steps bracketed by a barrier and a device synchronize, max over ranks.
+
+--impl reference times the reference's own CPU GEMM (test.cpp:19-30, restated in
+oracle/ because the reference needs ROCm + an MI355X) on this machine's host cores.
+"""
+from __future__ import annotations
+
+import argparse
+import datetime
+import json
+import math
+import os
+import statistics
+import sys
+import threading
+import time
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+if ROOT not in sys.path:
+    sys.path.insert(0, ROOT)
+
+WORKLOADS = {
+    # name: (M, N, K, stddev of B)  -- A is always N(0, 1)
+    "8192": (8192, 8192, 8192, 1.0),          # headline config
+    "4096": (4096, 4096, 4096, 1.0),          # configs[1]
+    "ffn": (16384, 28672, 8192, 0.02),        # configs[3]
+    "skinny128": (128, 8192, 8192, 1.0),      # configs[4]
+    "1024x7168x2048": (1024, 7168, 2048, 1.0),
+    "4000x5120x7168": (4000, 5120, 7168, 1.0),
+    "512": (512, 512, 512, 1.0),              # configs[0] (the CPU-runnable case)
+}
+L2_BYTES = 126 * 2**20
+METRIC = "FP8 e4m3 GEMM TFLOP/s and % of dense FP8 peak"
+
+# DRAM bytes (read + write) of one launch of the GEMM kernel, from an ncu capture of
+# the same workload (see profiles/); keyed by (workload, gpus).  None = not captured.
+TRAFFIC_BYTES_PER_LAUNCH: dict[tuple[str, int], float] = {
+    ("8192", 1): 336.159e6 + 114.371e6,  # profiles/fp8_gemm_tn_8192_bn256_1cta.md
+}
+
+
+def parse_args():
+    ap = argparse.ArgumentParser(description=__doc__, formatter_class=argparse.RawDescriptionHelpFormatter)
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=200)
+    ap.add_argument("--warmup", type=int, default=20)
+    ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
+    ap.add_argument("--workload", choices=sorted(WORKLOADS), default="8192")
+    ap.add_argument("--config", default="auto")
+    ap.add_argument("--allgather", action="store_true", help="also time the NCCL all-gather of C (N > 1)")
+    ap.add_argument("--no-cublas", action="store_true", help="skip the cuBLASLt comparison leg")
+    ap.add_argument("--no-cpu", action="store_true", help="skip the CPU baseline leg")
+    ap.add_argument("--seed", type=int, default=0)
+    return ap.parse_args()
+
+
+# ---------------------------------------------------------------------------------------
+# peaks and clocks
+
+def fp8_peak_tflops() -> tuple[float, str]:
+    """Dense FP8 roofline: twice the measured dense bf16 rate (tcgen05 runs kind::f8f6f4
+    at twice the kind::f16 rate), from MEASURED_PEAKS.json when present."""
+    path = os.path.join(ROOT, "MEASURED_PEAKS.json")
+    try:
+        with open(path) as f:
+            bf16 = float(json.load(f)["bf16_tflops"])
+        return 2.0 * bf16, "measured (2 x bf16_tflops of MEASURED_PEAKS.json)"
+    except Exception:
+        return 2.0 * 1590.0, "fallback (2 x 1590 TFLOP/s bf16)"
+
+
+_REASONS = [
+    (0x1, "gpu_idle"), (0x2, "applications_clocks_setting"), (0x4, "sw_power_cap"), (0x8, "hw_slowdown"),
+    (0x10, "sync_boost"), (0x20, "sw_thermal_slowdown"), (0x40, "hw_thermal_slowdown"),
+    (0x80, "hw_power_brake_slowdown"), (0x100, "display_clock_setting"),
+]
+
+
+class ClockSampler:
+    """Samples the SM clock and the clock-event reasons through NVML (what nvidia-smi
+    reads) every few milliseconds while the timed region runs."""
+
+    def __init__(self, torch_device_index: int, period_s: float = 0.005):
+        self.period = period_s
+        self.samples: list[tuple[int, int]] = []
+        self.error = None
+        self.max_mhz = None
+        self._stop = threading.Event()
+        self._thread = None
+        try:
+            import pynvml
+            import torch
+            pynvml.nvmlInit()
+            self.nv = pynvml
+            uuid = str(torch.cuda.get_device_properties(torch_device_index).uuid)
+            if not uuid.startswith("GPU-"):
+                uuid = "GPU-" + uuid
+            try:
+                self.h = pynvml.nvmlDeviceGetHandleByUUID(uuid)
+            except Exception:
+                vis = os.environ.get("CUDA_VISIBLE_DEVICES")
+                idx = int(vis.split(",")[torch_device_index]) if vis else torch_device_index
+                self.h = pynvml.nvmlDeviceGetHandleByIndex(idx)
+            self.max_mhz = int(pynvml.nvmlDeviceGetMaxClockInfo(self.h, pynvml.NVML_CLOCK_SM))
+        except Exception as e:  # no NVML: report it, do not guess
+            self.error = f"nvml unavailable: {e}"
+
+    def _reasons(self) -> int:
+        nv = self.nv
+        fn = getattr(nv, "nvmlDeviceGetCurrentClocksEventReasons", None) or nv.nvmlDeviceGetCurrentClocksThrottleReasons
+        return int(fn(self.h))
+
+    def _run(self):
+        while not self._stop.is_set():
+            try:
+                self.samples.append((int(self.nv.nvmlDeviceGetClockInfo(self.h, self.nv.NVML_CLOCK_SM)),
+                                     self._reasons()))
+            except Exception as e:
+                self.error = str(e)
+                return
+            time.sleep(self.period)
+
+    def start(self):
+        if self.error is None:
+            self._thread = threading.Thread(target=self._run, daemon=True)
+            self._thread.start()
+
+    def stop(self) -> dict:
+        if self._thread is not None:
+            self._stop.set()
+            self._thread.join()
+        if self.error is not None and not self.samples:
+            return {"unavailable": self.error}
+        mhz = [m for m, _ in self.samples]
+        mask = 0
+        for _, r in self.samples:
+            mask |= r
+        return {"sm_mhz": statistics.median(mhz) if mhz else None, "sm_max_mhz": self.max_mhz,
+                "reasons": [name for bit, name in _REASONS if mask & bit], "samples": len(mhz),
+                "source": "nvml"}
+
+
+# ---------------------------------------------------------------------------------------
+# CPU legs (the oracle restatement of test.cpp:19-30; bench's only use of oracle/)
+
+def cpu_reference_rate(M: int, N: int, K: int, std_b: float, seed: int, budget_s: float, steps: int = 1,
+                       warmup: int = 0) -> dict:
+    """Times the reference loop nest (OpenMP collapse(2), scalar fp32 accumulators) with
+    all host threads on a bounded sample of the workload: S rows x Ns columns x full K,
+    S chosen so each step takes about budget_s / (steps + warmup) seconds."""
+    import oracle
+    Ns = min(N, 2048)
+    rows_avail = min(M, 4096)
+    A, sa = oracle.make_quantized((rows_avail, K), seed)
+    B, sb = oracle.make_quantized((Ns, K), seed + 1, 0.0, std_b)
+    threads = oracle.max_threads()
+    t0 = time.perf_counter()
+    oracle.gemm_naive_rows(A, B, 0, 1, sa, sb)
+    t_row = max(time.perf_counter() - t0, 1e-6)
+    per_step = budget_s / max(1, steps + warmup)
+    S = int(max(1, min(rows_avail, per_step / t_row)))
+    times = []
+    for i in range(warmup + steps):
+        r0 = (i * S) % max(1, rows_avail - S + 1)
+        t0 = time.perf_counter()
+        oracle.gemm_naive_rows(A, B, r0, r0 + S, sa, sb)
+        dt = time.perf_counter() - t0
+        if i >= warmup:
+            times.append(dt)
+    mean = sum(times) / len(times)
+    flops = 2.0 * S * Ns * K
+    return {"value": flops / mean / 1e12, "unit": "TFLOP/s", "cores": threads, "kind": "port",
+            "sample": f"{S} rows x {Ns} cols x K={K} of the {M}x{N}x{K} workload per step, "
+                      f"{steps} timed steps, oracle_gemm_naive_rows (test.cpp:19-30 loop nest, OpenMP)",
+            "ms_per_step": mean * 1e3}
+
+
+def run_reference(args) -> None:
+    rank = int(os.environ.get("RANK", "0"))
+    if rank != 0:
+        return  # only rank 0 times the host CPU; the others exit without work
+    M, N, K, std_b = WORKLOADS[args.workload]
+    cb = cpu_reference_rate(M, N, K, std_b, args.seed, budget_s=90.0, steps=args.steps, warmup=args.warmup)
+    line = {
+        "impl": "reference", "metric": METRIC, "value": cb["value"], "unit": "TFLOP/s", "n_gpus": args.gpus,
+        "steps": args.steps, "warmup": args.warmup, "ms_per_step": cb["ms_per_step"], "higher_is_better": True,
+        "scaling": "strong", "vs_baseline": None, "dtype": "fp8e4m3", "data": "synthetic",
+        "config": {"workload": f"fp8_gemm_tn {M}x{N}x{K}", "M": M, "N": N, "K": K,
+                   "parallelism": "host CPU (rank 0 only)"},
+        "cpu_baseline": {k: cb[k] for k in ("value", "unit", "cores", "kind", "sample")},
+        "e2e": {"value": cb["value"], "unit": "TFLOP/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }
+    print(json.dumps(line), flush=True)
+
+
+# ---------------------------------------------------------------------------------------
+# GPU arm
+
+def quantize_on_device(x, group=None):
+    """Per-tensor amax/448 quantisation (global amax across ranks for row shards)."""
+    import torch
+
+    from hipgemm_b200.shard import global_amax_scale
+    scale = global_amax_scale(x, group)
+    q = (x / scale).to(torch.float8_e4m3fn)
+    return q.view(torch.uint8), scale
+
+
+def run_ours(args) -> None:
+    import torch
+    import torch.distributed as dist
+
+    import hipgemm_b200 as hg
+    from hipgemm_b200.shard import ShardedGemm
+
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local_rank = int(os.environ.get("LOCAL_RANK", "0"))
+    torch.cuda.set_device(local_rank)
+    dev = torch.device("cuda", local_rank)
+    if world > 1:
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=180), device_id=dev)
+    if args.gpus != world:
+        raise SystemExit(f"--gpus {args.gpus} but WORLD_SIZE={world}: launch N>1 with torchrun")
+
+    M, N, K, std_b = WORKLOADS[args.workload]
+    names = hg.config_names()
+    config = 0 if args.config == "auto" else names.index(args.config)
+    sg = ShardedGemm(M, N, K)
+    m = sg.rows
+    set_bytes = m * K + N * K
+    nbuf = int(min(16, max(2, math.ceil(4 * L2_BYTES / set_bytes))))
+
+    # Seeded synthetic inputs, quantised per tensor (amax/448); B identical on every rank.
+    A, B, SA, SB = [], [], [], []
+    for j in range(nbuf):
+        g = torch.Generator(device=dev)
+        g.manual_seed(args.seed + 2 * j * 1000003 + 7919 * rank)
+        xa = torch.randn((m, K), generator=g, device=dev, dtype=torch.float32)
+        qa, sa = quantize_on_device(xa)
+        del xa
+        g.manual_seed(args.seed + 2 * j * 1000003 + 1)
+        xb = torch.randn((N, K), generator=g, device=dev, dtype=torch.float32) * std_b
+        qb, sb = quantize_on_device(xb)
+        del xb
+        A.append(qa); B.append(qb); SA.append(sa); SB.append(sb)
+    C = torch.empty((m, N), dtype=torch.bfloat16, device=dev)
+    torch.cuda.synchronize()
+
+    def barrier():
+        if world > 1:
+            dist.barrier(device_ids=[local_rank])
+
+    def max_over_ranks(x: float) -> float:
+        if world == 1:
+            return x
+        t = torch.tensor([x], dtype=torch.float64, device=dev)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        return float(t.item())
+
+    def timed(fn, steps, warmup, sampler=None):
+        for i in range(warmup):
+            fn(i)
+        torch.cuda.synchronize()
+        barrier()
+        torch.cuda.synchronize()
+        stream = torch.cuda.current_stream()
+        e0 = torch.cuda.Event(enable_timing=True)
+        e1 = torch.cuda.Event(enable_timing=True)
+        if sampler:
+            sampler.start()
+        e0.record(stream)
+        for i in range(steps):
+            fn(warmup + i)
+        e1.record(stream)
+        torch.cuda.synchronize()
+        clocks = sampler.stop() if sampler else None
+        barrier()
+        torch.cuda.synchronize()
+        return max_over_ranks(e0.elapsed_time(e1) / steps), clocks
+
+    def gemm_step(i):
+        j = i % nbuf
+        sg.run(A[j], B[j], SA[j], SB[j], out=C, config=config)
+
+    sampler = ClockSampler(local_rank)
+    ms, clocks = timed(gemm_step, args.steps, args.warmup, sampler)
+    status = hg.device_status()
+    if status != 0:
+        raise SystemExit(f"kernel status word {status:#x}: a bounded wait expired")
+
+    flops_total = 2.0 * M * N * K
+    flops_rank = 2.0 * m * N * K
+    value = flops_total / (ms * 1e-3) / 1e12
+    peak, peak_src = fp8_peak_tflops()
+    achieved = flops_rank / (ms * 1e-3) / 1e12  # one launch per step on this rank
+    traffic = TRAFFIC_BYTES_PER_LAUNCH.get((args.workload, world))
+
+    extra = {}
+    if not args.no_cublas:
+        def lt_step(i):
+            j = i % nbuf
+            torch._scaled_mm(A[j].view(torch.float8_e4m3fn), B[j].view(torch.float8_e4m3fn).t(), scale_a=SA[j],
+                             scale_b=SB[j], out_dtype=torch.bfloat16)
+        ms_lt, _ = timed(lt_step, args.steps, max(3, args.warmup))
+        extra["cublaslt_fp8"] = {"value": flops_total / (ms_lt * 1e-3) / 1e12, "unit": "TFLOP/s",
+                                 "ms_per_step": ms_lt, "what": "torch._scaled_mm (cuBLASLt), same inputs"}
+
+    # End to end through the public API: pinned host A/B in, GEMM, C back to pinned host.
+    hA = A[0].cpu().pin_memory()
+    hB = B[0].cpu().pin_memory()
+    hS = torch.cat([SA[0], SB[0]]).cpu().pin_memory()
+    hC = torch.empty((m, N), dtype=torch.bfloat16).pin_memory()
+    dA = torch.empty_like(A[0])
+    dB = torch.empty_like(B[0])
+    dS = torch.empty(2, dtype=torch.float32, device=dev)
+
+    def e2e_step(i):
+        dA.copy_(hA, non_blocking=True)
+        dB.copy_(hB, non_blocking=True)
+        dS.copy_(hS, non_blocking=True)
+        sg.run(dA, dB, dS[0:1], dS[1:2], out=C, config=config)
+        hC.copy_(C, non_blocking=True)
+
+    e2e_steps = max(1, min(args.steps, 50))
+    ms_e2e, _ = timed(e2e_step, e2e_steps, 2)
+    e2e = {"value": flops_total / (ms_e2e * 1e-3) / 1e12, "unit": "TFLOP/s",
+           "h2d_bytes_per_step": int(hA.numel() + hB.numel() + 4 * hS.numel()),
+           "d2h_bytes_per_step": int(2 * hC.numel()), "steps": e2e_steps, "ms_per_step": ms_e2e}
+
+    if args.allgather and world > 1:
+        gathered = sg.gather_buffer(dev)
+        ms_ag, _ = timed(lambda i: sg.all_gather(C, gathered), args.steps, 3)
+        extra["allgather"] = {"ms_per_step": ms_ag, "bytes": int(2 * M * N), "what": "NCCL all_gather of bf16 C"}
+
+    cpu = None
+    if rank == 0 and world == 1 and not args.no_cpu:
+        cpu = cpu_reference_rate(M, N, K, std_b, args.seed, budget_s=15.0, steps=3, warmup=1)
+        cpu.pop("ms_per_step", None)
+
+    if rank == 0:
+        line = {
+            "metric": METRIC, "value": value, "unit": "TFLOP/s", "n_gpus": world, "steps": args.steps,
+            "warmup": args.warmup, "ms_per_step": ms, "higher_is_better": True, "scaling": "strong",
+            "vs_baseline": None, "dtype": "fp8e4m3", "data": "synthetic",
+            "config": {"workload": f"fp8_gemm_tn {M}x{N}x{K}", "M": M, "N": N, "K": K, "rows_per_gpu": m,
+                       "parallelism": f"m-shard{world}, B replicated", "tile_config": args.config,
+                       "inputs": f"seeded N(0,1) A, N(0,{std_b}) B, per-tensor amax/448 e4m3",
+                       "l2": f"rotating inputs: {nbuf} (A,B) sets = {nbuf * set_bytes / 2**20:.0f} MiB per GPU "
+                             f"> 126 MB L2"},
+            "pct_dense_fp8_peak": 100.0 * value / (world * peak),
+            "roofline": {"bound": "tensor", "achieved": achieved, "peak": peak, "unit": "TFLOP/s",
+                         "frac": achieved / peak, "traffic": traffic, "peak_source": peak_src,
+                         "kernel": "hg::fp8_gemm_tn_sm100 (per-GPU launch, CUDA events on its stream)"},
+            "cpu_baseline": cpu,
+            "e2e": e2e,
+            "gpu_launches": args.steps,
+            "clocks": clocks,
+        }
+        line.update(extra)
+        print(json.dumps(line), flush=True)
+
+    if world > 1:
+        dist.destroy_process_group()
+
+
+def main():
+    args = parse_args()
+    if args.impl == "reference":
+        run_reference(args)
+    else:
+        run_ours(args)
+
+
+if __name__ == "__main__":
+    main()

@@ -37,6 +37,7 @@ _SIGNATURES = {
     "hgemm_fp8_tn_rows": (_i, [_vp, _vp, _vp, _i, _i, _i, _i, _i, _vp, _vp, _vp]),
     "hgemm_fp8_tn_config": (_i, [_vp, _vp, _vp, _i, _i, _i, _vp, _vp, _vp, _i]),
     "hgemm_num_configs": (_i, []),
+    "hgemm_config_resident_ctas": (_i, [_i]),
     "hgemm_config_name": (ctypes.c_char_p, [_i]),
     "hgemm_device_status": (_i, [ctypes.POINTER(ctypes.c_uint32)]),
     "hgemm_error_string": (ctypes.c_char_p, [_i]),

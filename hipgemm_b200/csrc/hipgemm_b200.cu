@@ -25,10 +25,16 @@ using EncodeTiledFn = CUresult (*)(CUtensorMap*, CUtensorMapDataType, cuuint32_t
 
 constexpr int kMaxDevices = 64;
 
+constexpr int kMaxConfigs = 16;
+
 struct DeviceState {
     std::once_flag once;
     int status = HGEMM_ERR_NO_DEVICE;
     int num_sms = 0;
+    // Persistent grid size per configuration: CTAs that can be resident at once.  For
+    // CTA pairs this comes from cudaOccupancyMaxActiveClusters, which can be below
+    // num_sms / 2 (clusters must fit inside one GPC).
+    int resident_ctas[kMaxConfigs] = {};
 };
 
 DeviceState g_devices[kMaxDevices];
@@ -39,7 +45,11 @@ EncodeTiledFn g_encode = nullptr;
 
 struct KernelConfig {
     const char* name;
-    int bn;
+    int bm;          // output tile rows (256 for a CTA pair)
+    int bn;          // output tile columns
+    int ctas;        // CTAs per tile (2 = cta_group::2 pair)
+    int b_box_rows;  // rows of B one CTA loads per K block
+    double eff;      // relative per-SM efficiency used by the automatic choice
     int smem_bytes;
     const void* kernel;  // __global__ function pointer
     int (*launch)(const CUtensorMap&, const CUtensorMap&, const CUtensorMap&, const GemmParams&, int grid,
@@ -55,16 +65,34 @@ int launch_1cta(const CUtensorMap& ta, const CUtensorMap& tb, const CUtensorMap&
 }
 
 template <int BN, int STAGES>
-KernelConfig make_1cta(const char* name) {
-    return KernelConfig{name, BN, GemmConfig<BN, STAGES>::SMEM_BYTES,
+KernelConfig make_1cta(const char* name, double eff) {
+    return KernelConfig{name, 128, BN, 1, BN, eff, GemmConfig<BN, STAGES>::SMEM_BYTES,
                         reinterpret_cast<const void*>(&fp8_gemm_tn_sm100<BN, STAGES>), &launch_1cta<BN, STAGES>};
 }
 
+template <int BN, int STAGES>
+int launch_pair(const CUtensorMap& ta, const CUtensorMap& tb, const CUtensorMap& tc, const GemmParams& p, int grid,
+                cudaStream_t stream) {
+    using Cfg = PairConfig<BN, STAGES>;
+    // The cluster shape (2, 1, 1) is compiled into the kernel; grid is a multiple of 2.
+    fp8_gemm_tn_sm100_pair<BN, STAGES><<<grid, Cfg::kNumThreads, Cfg::SMEM_BYTES, stream>>>(ta, tb, tc, p);
+    return cudaGetLastError() == cudaSuccess ? HGEMM_OK : HGEMM_ERR_CUDA;
+}
+
+template <int BN, int STAGES>
+KernelConfig make_pair(const char* name, double eff) {
+    return KernelConfig{name, 256, BN, 2, BN / 2, eff, PairConfig<BN, STAGES>::SMEM_BYTES,
+                        reinterpret_cast<const void*>(&fp8_gemm_tn_sm100_pair<BN, STAGES>),
+                        &launch_pair<BN, STAGES>};
+}
+
 const KernelConfig kConfigs[] = {
-    {"auto", 0, 0, nullptr, nullptr},
-    make_1cta<256, 4>("bn256_s4"),
-    make_1cta<128, 6>("bn128_s6"),
-    make_1cta<64, 8>("bn64_s8"),
+    {"auto", 0, 0, 0, 0, 0.0, 0, nullptr, nullptr},
+    make_1cta<256, 4>("bn256_s4", 0.93),
+    make_1cta<128, 6>("bn128_s6", 0.80),
+    make_1cta<64, 8>("bn64_s8", 0.45),
+    make_pair<256, 6>("pair256_s6", 1.0),
+    make_pair<128, 8>("pair128_s8", 0.85),
 };
 constexpr int kNumConfigs = sizeof(kConfigs) / sizeof(kConfigs[0]);
 
@@ -89,12 +117,36 @@ int device_setup(int dev) {
             st.status = HGEMM_ERR_CUDA;
             return;
         }
+        static_assert(kNumConfigs <= kMaxConfigs, "raise kMaxConfigs");
         for (int c = 1; c < kNumConfigs; ++c) {
-            if (cudaFuncSetAttribute(kConfigs[c].kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                     kConfigs[c].smem_bytes) != cudaSuccess) {
+            const KernelConfig& k = kConfigs[c];
+            if (cudaFuncSetAttribute(k.kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, k.smem_bytes) !=
+                cudaSuccess) {
                 st.status = HGEMM_ERR_CUDA;
                 return;
             }
+            if (k.ctas == 1) {
+                st.resident_ctas[c] = prop.multiProcessorCount;
+                continue;
+            }
+            cudaLaunchConfig_t cfg{};
+            cudaLaunchAttribute attr[1];
+            attr[0].id = cudaLaunchAttributeClusterDimension;
+            attr[0].val.clusterDim.x = k.ctas;
+            attr[0].val.clusterDim.y = 1;
+            attr[0].val.clusterDim.z = 1;
+            cfg.gridDim = dim3(static_cast<unsigned>(k.ctas * (prop.multiProcessorCount / k.ctas)), 1, 1);
+            cfg.blockDim = dim3(192, 1, 1);
+            cfg.dynamicSmemBytes = static_cast<size_t>(k.smem_bytes);
+            cfg.attrs = attr;
+            cfg.numAttrs = 1;
+            int clusters = 0;
+            if (cudaOccupancyMaxActiveClusters(&clusters, k.kernel, &cfg) != cudaSuccess || clusters <= 0) {
+                cudaGetLastError();
+                st.status = HGEMM_ERR_CUDA;
+                return;
+            }
+            st.resident_ctas[c] = clusters * k.ctas;
         }
         st.num_sms = prop.multiProcessorCount;
         st.status = HGEMM_OK;
@@ -102,15 +154,15 @@ int device_setup(int dev) {
     return st.status;
 }
 
-int current_device_setup(int* num_sms) {
+const DeviceState* current_device_setup(int* rc) {
     int dev = -1;
     if (cudaGetDevice(&dev) != cudaSuccess) {
         cudaGetLastError();
-        return HGEMM_ERR_NO_DEVICE;
+        *rc = HGEMM_ERR_NO_DEVICE;
+        return nullptr;
     }
-    const int rc = device_setup(dev);
-    if (rc == HGEMM_OK) *num_sms = g_devices[dev].num_sms;
-    return rc;
+    *rc = device_setup(dev);
+    return *rc == HGEMM_OK ? &g_devices[dev] : nullptr;
 }
 
 bool encode_2d(CUtensorMap* map, CUtensorMapDataType dtype, size_t elem_bytes, const void* ptr, uint64_t inner,
@@ -124,18 +176,18 @@ bool encode_2d(CUtensorMap* map, CUtensorMapDataType dtype, size_t elem_bytes, c
                     CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
 }
 
-// Estimated relative time of a 1-CTA configuration: waves of 128 x BN tiles over the
-// SMs, times the per-tile work, with a penalty for the narrower tiles (their MMAs
-// re-read the A tile from shared memory for fewer columns).
-int choose_config(int M, int N, int num_sms) {
+// Estimated relative time of a configuration: waves of output tiles over the SMs (CTA
+// pairs count as one tile slot per two SMs) times the per-SM share of one tile,
+// divided by the configuration's measured relative efficiency at large sizes.
+int choose_config(int M, int N, const DeviceState& dev) {
     int best = 1;
     double best_cost = 1e300;
     for (int c = 1; c < kNumConfigs; ++c) {
-        const int bn = kConfigs[c].bn;
-        const long tiles = static_cast<long>((M + 127) / 128) * ((N + bn - 1) / bn);
-        const long waves = (tiles + num_sms - 1) / num_sms;
-        const double eff = bn == 256 ? 1.0 : (bn == 128 ? 0.92 : 0.75);
-        const double cost = static_cast<double>(waves) * bn / eff;
+        const KernelConfig& k = kConfigs[c];
+        const long tiles = static_cast<long>((M + k.bm - 1) / k.bm) * ((N + k.bn - 1) / k.bn);
+        const long slots = std::max(1, dev.resident_ctas[c] / k.ctas);
+        const long waves = (tiles + slots - 1) / slots;
+        const double cost = static_cast<double>(waves) * (k.bm / k.ctas) * k.bn / k.eff;
         if (cost < best_cost - 1e-9) {
             best_cost = cost;
             best = c;
@@ -154,22 +206,22 @@ int run_gemm(const void* A, const void* B, void* C, int M, int N, int K, const f
     if (!C || (K > 0 && (!A || !B))) return HGEMM_ERR_INVALID_VALUE;
     if (K % 16 != 0 || N % 8 != 0) return HGEMM_ERR_ALIGNMENT;
     if (!aligned16(C) || (K > 0 && (!aligned16(A) || !aligned16(B)))) return HGEMM_ERR_ALIGNMENT;
-    int num_sms = 0;
-    const int rc = current_device_setup(&num_sms);
+    int rc = HGEMM_OK;
+    const DeviceState* dev = current_device_setup(&rc);
     if (rc != HGEMM_OK) return rc;
     if (K == 0) {
         // An empty sum: every element is bf16(+0), as the reference's acc = 0.0f gives.
         return cudaMemsetAsync(C, 0, static_cast<size_t>(M) * N * 2, stream) == cudaSuccess ? HGEMM_OK
                                                                                               : HGEMM_ERR_CUDA;
     }
-    const int c = config == 0 ? choose_config(M, N, num_sms) : config;
+    const int c = config == 0 ? choose_config(M, N, *dev) : config;
     const KernelConfig& kc = kConfigs[c];
 
     CUtensorMap ta, tb, tc;
     if (!encode_2d(&ta, CU_TENSOR_MAP_DATA_TYPE_UINT8, 1, A, static_cast<uint64_t>(K), static_cast<uint64_t>(M), 128,
                    128) ||
         !encode_2d(&tb, CU_TENSOR_MAP_DATA_TYPE_UINT8, 1, B, static_cast<uint64_t>(K), static_cast<uint64_t>(N), 128,
-                   static_cast<uint32_t>(kc.bn)) ||
+                   static_cast<uint32_t>(kc.b_box_rows)) ||
         !encode_2d(&tc, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, C, static_cast<uint64_t>(N), static_cast<uint64_t>(M), 64,
                    32)) {
         return HGEMM_ERR_CUDA;
@@ -178,14 +230,15 @@ int run_gemm(const void* A, const void* B, void* C, int M, int N, int K, const f
     p.M = M;
     p.N = N;
     p.K = K;
-    p.num_m_blocks = (M + 127) / 128;
+    p.num_m_blocks = (M + kc.bm - 1) / kc.bm;
     p.num_n_blocks = (N + kc.bn - 1) / kc.bn;
     p.num_k_blocks = (K + 127) / 128;
-    p.group_m = 16;
+    p.group_m = kc.ctas == 2 ? 8 : 16;
     p.scale_a = sa;
     p.scale_b = sb;
     const long tiles = static_cast<long>(p.num_m_blocks) * p.num_n_blocks;
-    const int grid = static_cast<int>(std::min<long>(tiles, num_sms));
+    const int slots = std::max(1, dev->resident_ctas[c] / kc.ctas);
+    const int grid = static_cast<int>(std::min<long>(tiles, slots)) * kc.ctas;
     return kc.launch(ta, tb, tc, p, grid, stream);
 }
 
@@ -218,6 +271,13 @@ int hgemm_fp8_tn_rows(const void* A, const void* B, void* C, int M, int N, int K
 }
 
 int hgemm_num_configs(void) { return hg::kNumConfigs; }
+
+int hgemm_config_resident_ctas(int config) {
+    if (config <= 0 || config >= hg::kNumConfigs) return HGEMM_ERR_INVALID_VALUE;
+    int rc = HGEMM_OK;
+    const hg::DeviceState* dev = hg::current_device_setup(&rc);
+    return dev ? dev->resident_ctas[config] : rc;
+}
 
 const char* hgemm_config_name(int config) {
     if (config < 0 || config >= hg::kNumConfigs) return nullptr;

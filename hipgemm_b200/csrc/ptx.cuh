@@ -55,9 +55,15 @@ __device__ __forceinline__ void mbar_arrive(uint32_t bar) {
     asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(bar) : "memory");
 }
 
-// Arrive on an mbarrier of another CTA of the cluster (address from mapa).
+// Arrive on an mbarrier of another CTA of the cluster (address from mapa), default
+// (CTA-scope release) semantics.  A cluster-scope release here made the issuing thread
+// wait for its own outstanding memory operations, which for the TMA producer put one
+// full load latency on every pipeline stage (the pair kernel ran at half speed).  The
+// signals sent this way carry no data of the sending thread: they report completions
+// (tensor-core reads of a stage, tensor-memory reads of an accumulator) that the
+// sender has already observed through an mbarrier or tcgen05.wait.
 __device__ __forceinline__ void mbar_arrive_cluster(uint32_t cluster_bar) {
-    asm volatile("mbarrier.arrive.release.cluster.shared::cluster.b64 _, [%0];" ::"r"(cluster_bar) : "memory");
+    asm volatile("mbarrier.arrive.shared::cluster.b64 _, [%0];" ::"r"(cluster_bar) : "memory");
 }
 
 __device__ __forceinline__ bool mbar_try_wait(uint32_t bar, uint32_t parity) {

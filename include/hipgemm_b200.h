@@ -68,6 +68,9 @@ int hgemm_fp8_tn_config(const void* A, const void* B, void* C, int M, int N, int
 /* Number of tile configurations and their names ("bn256_s4" ...); NULL past the end. */
 int hgemm_num_configs(void);
 const char* hgemm_config_name(int config);
+/* Synchronous (device set-up).  CTAs of configuration `config` (>= 1) that the current
+ * device keeps resident at once, i.e. the persistent grid size; negative on error. */
+int hgemm_config_resident_ctas(int config);
 
 /* Synchronous.  Reads and clears the current device's kernel status word: 0 when no
  * bounded wait has expired since the last call, else the code of the first one. */

@@ -74,9 +74,10 @@ def test_ragged_tails(cuda_device, M, N, K):
     _run(M, N, K, seed_a=M, seed_b=N + K)
 
 
-@pytest.mark.parametrize("config", [1, 2, 3])
-def test_every_tile_config(cuda_device, config):
-    _run(391, 648, 784, config=config)
+@pytest.mark.parametrize("config", [1, 2, 3, 4, 5])
+@pytest.mark.parametrize("M,N,K", [(391, 648, 784), (1000, 1032, 2064), (2048, 2048, 1024)])
+def test_every_tile_config(cuda_device, config, M, N, K):
+    _run(M, N, K, config=config)
 
 
 def test_unscaled_and_one_scale(cuda_device):

@@ -48,6 +48,7 @@ _SIGNATURES = {
     "hgemm_host_quantize_e4m3": (ctypes.c_float, [_vp, ctypes.c_size_t, _vp]),
     "hgemm_host_fp8_encode": (ctypes.c_uint8, [ctypes.c_float]),
     "hgemm_host_bf16_rne": (ctypes.c_uint16, [ctypes.c_float]),
+    "hgemm_host_fp8_encode_array": (None, [_vp, ctypes.c_size_t, _vp]),
 }
 
 

@@ -314,6 +314,10 @@ uint8_t hgemm_host_fp8_encode(float x) {
     return static_cast<uint8_t>(__nv_cvt_float_to_fp8(x, __NV_SATFINITE, __NV_E4M3));
 }
 
+void hgemm_host_fp8_encode_array(const float* x, size_t n, uint8_t* out) {
+    for (size_t i = 0; i < n; ++i) out[i] = hgemm_host_fp8_encode(x[i]);
+}
+
 uint16_t hgemm_host_bf16_rne(float x) {
     const __nv_bfloat16 b = __float2bfloat16_rn(x);
     uint16_t bits;

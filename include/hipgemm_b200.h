@@ -101,6 +101,8 @@ float hgemm_host_quantize_e4m3(const float* x, size_t n, uint8_t* q);
 /* One value through CUDA's host e4m3 / bf16 conversions (for checks). */
 uint8_t hgemm_host_fp8_encode(float x);
 uint16_t hgemm_host_bf16_rne(float x);
+/* n values through CUDA's host e4m3 conversion (satfinite, RNE). */
+void hgemm_host_fp8_encode_array(const float* x, size_t n, uint8_t* out);
 
 #ifdef __cplusplus
 } /* extern "C" */

@@ -24,6 +24,8 @@ _f = ctypes.c_float
 _SIG = {
     "oracle_fp8_encode": (ctypes.c_uint8, [_f]),
     "oracle_fp8_decode": (_f, [ctypes.c_uint8]),
+    "oracle_fp8_encode_array": (None, [_vp, ctypes.c_size_t, _vp]),
+    "oracle_bf16_rne_array": (None, [_vp, ctypes.c_size_t, _vp]),
     "oracle_bf16_rne": (ctypes.c_uint16, [_f]),
     "oracle_bf16_to_float": (_f, [ctypes.c_uint16]),
     "oracle_normal_f32": (None, [_vp, ctypes.c_size_t, ctypes.c_uint64, _f, _f]),
@@ -74,6 +76,20 @@ def fp8_encode(x: float) -> int:
 
 def fp8_decode(b: int) -> float:
     return float(lib().oracle_fp8_decode(int(b)))
+
+
+def fp8_encode_array(x: np.ndarray) -> np.ndarray:
+    x = np.ascontiguousarray(x, dtype=np.float32)
+    out = np.empty(x.shape, dtype=np.uint8)
+    lib().oracle_fp8_encode_array(_p(x), x.size, _p(out))
+    return out
+
+
+def bf16_rne_array(x: np.ndarray) -> np.ndarray:
+    x = np.ascontiguousarray(x, dtype=np.float32)
+    out = np.empty(x.shape, dtype=np.uint16)
+    lib().oracle_bf16_rne_array(_p(x), x.size, _p(out))
+    return out
 
 
 def decode_table() -> np.ndarray:

@@ -152,6 +152,12 @@ void gemm_rows_impl(const uint8_t* A, const uint8_t* B, uint16_t* C, int ldc, in
 extern "C" {
 
 uint8_t oracle_fp8_encode(float x) { return encode_e4m3(x); }
+void oracle_fp8_encode_array(const float* x, size_t n, uint8_t* out) {
+    for (size_t i = 0; i < n; ++i) out[i] = encode_e4m3(x[i]);
+}
+void oracle_bf16_rne_array(const float* x, size_t n, uint16_t* out) {
+    for (size_t i = 0; i < n; ++i) out[i] = bf16_rne(x[i]);
+}
 float oracle_fp8_decode(uint8_t b) { return kDecode.v[b]; }
 uint16_t oracle_bf16_rne(float x) { return bf16_rne(x); }
 float oracle_bf16_to_float(uint16_t b) { return bf16_to_f32(b); }

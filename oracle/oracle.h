@@ -42,6 +42,8 @@ extern "C" {
 uint8_t oracle_fp8_encode(float x);
 /* Exact decode of one e4m3 byte.  Call site: test.cpp:25 `float(A[...])`. */
 float oracle_fp8_decode(uint8_t b);
+void oracle_fp8_encode_array(const float* x, size_t n, uint8_t* out);
+void oracle_bf16_rne_array(const float* x, size_t n, uint16_t* out);
 /* fp32 -> bf16 bits, round-to-nearest-even (NaN stays NaN).  Call site: test.cpp:27. */
 uint16_t oracle_bf16_rne(float x);
 float oracle_bf16_to_float(uint16_t b);

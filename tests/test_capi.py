@@ -1,0 +1,106 @@
+"""CPU checks of the C ABI (no GPU needed): the library loads, exports every function
+include/hipgemm_b200.h declares, rejects bad arguments before touching a device, and the
+header-only drop-in for fp8_gemm_4wave_256x256x128<M,N,K> (fp8_4wave.hpp:334-338)
+compiles as C++ and as plain C (the extern "C" part)."""
+import ctypes
+import os
+import re
+import subprocess
+
+import pytest
+
+import hipgemm_b200 as hg
+
+ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+HEADER = os.path.join(ROOT, "include", "hipgemm_b200.h")
+
+
+def declared_functions() -> list[str]:
+    text = open(HEADER).read()
+    text = re.sub(r"/\*.*?\*/", "", text, flags=re.S)
+    return sorted(set(re.findall(r"\b(hgemm_\w+)\s*\(", text)) - {"hgemm_stream_t"})
+
+
+def test_every_declared_symbol_is_exported():
+    names = declared_functions()
+    assert "hgemm_fp8_tn" in names and "hgemm_fp8_tn_rows" in names
+    lib = ctypes.CDLL(hg.LIB_PATH)
+    missing = [n for n in names if not hasattr(lib, n)]
+    assert not missing, missing
+
+
+def test_library_metadata():
+    L = hg.lib()
+    assert L.hgemm_version().decode().startswith("hipgemm_b200")
+    names = hg.config_names()
+    assert names[0] == "auto" and {"bn256_s4", "pair256_s6"} <= set(names)
+    assert L.hgemm_config_name(len(names)) is None
+    for code in range(0, -7, -1):
+        assert L.hgemm_error_string(code)
+
+
+FAKE = 0x10000  # 16-byte aligned, never dereferenced: the checks fail before any CUDA call
+
+
+@pytest.mark.parametrize("args,code", [
+    ((FAKE, FAKE, FAKE, -1, 8, 16), hg.HGEMM_ERR_INVALID_VALUE),
+    ((FAKE, FAKE, FAKE, 8, -8, 16), hg.HGEMM_ERR_INVALID_VALUE),
+    ((FAKE, FAKE, FAKE, 8, 8, -16), hg.HGEMM_ERR_INVALID_VALUE),
+    ((FAKE, FAKE, None, 8, 8, 16), hg.HGEMM_ERR_INVALID_VALUE),
+    ((None, FAKE, FAKE, 8, 8, 16), hg.HGEMM_ERR_INVALID_VALUE),
+    ((FAKE, None, FAKE, 8, 8, 16), hg.HGEMM_ERR_INVALID_VALUE),
+    ((FAKE, FAKE, FAKE, 8, 8, 24), hg.HGEMM_ERR_ALIGNMENT),      # K % 16
+    ((FAKE, FAKE, FAKE, 8, 12, 16), hg.HGEMM_ERR_ALIGNMENT),     # N % 8
+    ((FAKE + 1, FAKE, FAKE, 8, 8, 16), hg.HGEMM_ERR_ALIGNMENT),  # misaligned A
+    ((FAKE, FAKE + 8, FAKE, 8, 8, 16), hg.HGEMM_ERR_ALIGNMENT),  # misaligned B
+    ((FAKE, FAKE, FAKE + 2, 8, 8, 16), hg.HGEMM_ERR_ALIGNMENT),  # misaligned C
+    ((None, None, None, 0, 8, 16), hg.HGEMM_OK),                 # M == 0: nothing to do
+    ((None, None, None, 8, 0, 16), hg.HGEMM_OK),                 # N == 0
+])
+def test_argument_checks_without_device(args, code):
+    A, B, C, M, N, K = args
+    assert hg.lib().hgemm_fp8_tn(A, B, C, M, N, K, None, None, None) == code
+
+
+def test_config_and_row_range_checks():
+    L = hg.lib()
+    assert L.hgemm_fp8_tn_config(FAKE, FAKE, FAKE, 8, 8, 16, None, None, None, 99) == hg.HGEMM_ERR_INVALID_VALUE
+    assert L.hgemm_fp8_tn_config(FAKE, FAKE, FAKE, 8, 8, 16, None, None, None, -1) == hg.HGEMM_ERR_INVALID_VALUE
+    assert L.hgemm_fp8_tn_rows(FAKE, FAKE, FAKE, 8, 8, 16, 5, 3, None, None, None) == hg.HGEMM_ERR_INVALID_VALUE
+    assert L.hgemm_fp8_tn_rows(FAKE, FAKE, FAKE, 8, 8, 16, 0, 9, None, None, None) == hg.HGEMM_ERR_INVALID_VALUE
+    assert L.hgemm_fp8_tn_rows(FAKE, FAKE, FAKE, 8, 8, 16, -1, 3, None, None, None) == hg.HGEMM_ERR_INVALID_VALUE
+    assert L.hgemm_fp8_tn_rows(FAKE, FAKE, FAKE, 8, 8, 16, 4, 4, None, None, None) == hg.HGEMM_OK
+
+
+def test_python_wrapper_refuses_cpu_tensors():
+    import torch
+    a = torch.zeros((8, 16), dtype=torch.uint8)
+    with pytest.raises(ValueError, match="CUDA"):
+        hg.fp8_gemm_tn(a, a)
+    with pytest.raises(TypeError):
+        hg.fp8_gemm_tn(torch.zeros((8, 16), dtype=torch.float32), a)
+
+
+def test_header_compiles_as_cpp_and_c(tmp_path):
+    cpp = tmp_path / "use.cpp"
+    cpp.write_text(
+        '#include "hipgemm_b200.h"\n'
+        "int launch(const void* a, const void* b, void* c) {\n"
+        "  return fp8_gemm_4wave_256x256x128<4096, 4096, 4096>(a, b, c);\n"
+        "}\n")
+    c = tmp_path / "use.c"
+    c.write_text('#include "hipgemm_b200.h"\nint f(void) { return hgemm_fp8_tn(0, 0, 0, 0, 0, 0, 0, 0, 0); }\n')
+    for cmd in (["g++", "-std=c++17", "-Wall", "-Werror", "-fsyntax-only", "-I", os.path.dirname(HEADER), str(cpp)],
+                ["gcc", "-std=c99", "-Wall", "-Werror", "-fsyntax-only", "-I", os.path.dirname(HEADER), str(c)]):
+        r = subprocess.run(cmd, capture_output=True, text=True)
+        assert r.returncode == 0, r.stderr
+
+
+def test_header_template_rejects_bad_shapes(tmp_path):
+    cpp = tmp_path / "bad.cpp"
+    cpp.write_text('#include "hipgemm_b200.h"\n'
+                   "int f(const void* a, const void* b, void* c) {\n"
+                   "  return fp8_gemm_4wave_256x256x128<256, 256, 200>(a, b, c);\n}\n")
+    r = subprocess.run(["g++", "-std=c++17", "-fsyntax-only", "-I", os.path.dirname(HEADER), str(cpp)],
+                       capture_output=True, text=True)
+    assert r.returncode != 0 and "multiple of 16" in r.stderr

@@ -1,0 +1,200 @@
+"""CPU checks of the oracle (the restatement of test.cpp:19-47 and utils.hpp:27-33):
+known answers from the OCP FP8 spec and the C++ standard, a bit-for-bit sweep against
+CUDA's host e4m3 conversion, bf16 rounding against torch, and the GEMM loop against an
+independent numpy restatement and the committed golden fixtures."""
+import glob
+import os
+
+import numpy as np
+import pytest
+import torch
+
+import oracle
+
+GOLDEN = sorted(glob.glob(os.path.join(os.path.dirname(__file__), "golden", "*.npz")))
+
+
+# ---- fp8 e4m3 -----------------------------------------------------------------------------
+
+@pytest.mark.parametrize("code,value", [
+    (0x00, 0.0), (0x01, 2.0 ** -9), (0x07, 7 * 2.0 ** -9), (0x08, 2.0 ** -6), (0x38, 1.0), (0x39, 1.125),
+    (0x3C, 1.5), (0x40, 2.0), (0x7E, 448.0), (0x77, 240.0), (0xB8, -1.0), (0xFE, -448.0), (0x80, -0.0),
+])
+def test_e4m3_decode_known_values(code, value):
+    got = oracle.fp8_decode(code)
+    assert got == value and np.signbit(got) == np.signbit(value)
+
+
+def test_e4m3_nan_codes():
+    assert np.isnan(oracle.fp8_decode(0x7F)) and np.isnan(oracle.fp8_decode(0xFF))
+
+
+def test_e4m3_round_trip_all_codes():
+    for b in range(256):
+        if b in (0x7F, 0xFF):
+            continue
+        assert oracle.fp8_encode(oracle.fp8_decode(b)) == b, hex(b)
+
+
+@pytest.mark.parametrize("x,code", [
+    (1.0625, 0x38), (1.1875, 0x3A), (-1.0625, 0xB8),           # ties go to the even mantissa
+    (2.0 ** -10, 0x00), (1.5 * 2 ** -9, 0x02), (2.5 * 2 ** -9, 0x02),  # subnormal ties
+    (449.0, 0x7E), (464.0, 0x7E), (470.0, 0x7E), (1e30, 0x7E), (float("inf"), 0x7E),  # saturate to finite
+    (-1e30, 0xFE), (float("-inf"), 0xFE), (2.0 ** -30, 0x00), (-(2.0 ** -30), 0x80),
+])
+def test_e4m3_encode_rounding_and_saturation(x, code):
+    assert oracle.fp8_encode(x) == code
+
+
+def test_e4m3_encode_nan():
+    assert oracle.fp8_encode(float("nan")) & 0x7F == 0x7F
+
+
+def _sweep_floats() -> np.ndarray:
+    """Every fp8 midpoint and its fp32 neighbours, plus a strided sweep of all fp32
+    bit patterns with exponents from 2^-12 to 2^10, both signs."""
+    vals = np.array([oracle.fp8_decode(b) for b in range(0x7F)], dtype=np.float64)
+    mids = (vals[:-1] + vals[1:]) / 2
+    mids = np.concatenate([mids, [464.0, 448.0]]).astype(np.float32)
+    u = mids.view(np.uint32)
+    near = np.concatenate([u - 1, u, u + 1]).view(np.float32)
+    lo = np.float32(2.0 ** -12).view(np.uint32)
+    hi = np.float32(2.0 ** 10).view(np.uint32)
+    strided = np.arange(lo, hi, 97, dtype=np.uint32).view(np.float32)
+    x = np.concatenate([near, strided, [0.0, np.inf]]).astype(np.float32)
+    return np.concatenate([x, -x])
+
+
+def test_e4m3_encode_matches_cuda_host_conversion():
+    """Oracle encoder vs CUDA's __nv_cvt_float_to_fp8(x, __NV_SATFINITE, __NV_E4M3),
+    called through the product library's host utility, bit for bit."""
+    import hipgemm_b200 as hg
+    x = _sweep_floats()
+    ours = oracle.fp8_encode_array(x)
+    cuda = np.empty_like(ours)
+    hg.lib().hgemm_host_fp8_encode_array(x.ctypes.data, x.size, cuda.ctypes.data)
+    bad = np.nonzero(ours != cuda)[0]
+    assert bad.size == 0, f"{bad.size} differences, first x={x[bad[0]]!r}: oracle {ours[bad[0]]:#x} cuda {cuda[bad[0]]:#x}"
+    assert x.size > 2_000_000
+
+
+def test_e4m3_encode_matches_torch_in_range():
+    """torch's float8_e4m3fn cast (RNE, no saturation) agrees wherever |x| < 464."""
+    x = _sweep_floats()
+    x = x[np.abs(x) < 464.0]
+    t = torch.from_numpy(x).to(torch.float8_e4m3fn).view(torch.uint8).numpy()
+    assert np.array_equal(oracle.fp8_encode_array(x), t)
+
+
+# ---- bf16 ----------------------------------------------------------------------------------
+
+def test_bf16_rne_matches_torch_and_cuda():
+    import hipgemm_b200 as hg
+    rng = np.random.default_rng(0)
+    x = np.concatenate([
+        rng.standard_normal(200_000).astype(np.float32) * 1000,
+        (rng.integers(0, 2 ** 16, 50_000, dtype=np.uint32) << 16 | 0x8000).view(np.float32),  # exact ties
+        np.array([0.0, -0.0, 1.0, 65504.0, 3.3895314e38, np.float32(2 ** -133)], dtype=np.float32),
+    ]).astype(np.float32)
+    x = x[np.isfinite(x)]
+    ours = oracle.bf16_rne_array(x)
+    t = torch.from_numpy(x).to(torch.bfloat16).view(torch.int16).numpy().view(np.uint16)
+    assert np.array_equal(ours, t)
+    for v in x[:2000]:
+        assert hg.lib().hgemm_host_bf16_rne(float(v)) == oracle.bf16_rne(float(v))
+
+
+# ---- generator -------------------------------------------------------------------------------
+
+def test_mt19937_known_answer():
+    assert oracle.mt19937_nth(5489, 10000) == 4123659995  # C++ [rand.predef]
+
+
+def test_reference_generator_defaults():
+    """utils.hpp:27-33: seed 0, N(-1, 1), cast straight to e4m3; deterministic and
+    matching the product's host mirror byte for byte."""
+    import hipgemm_b200 as hg
+    a = oracle.init_random_fp8(1 << 16, 0, -1.0, 1.0)
+    b = oracle.init_random_fp8(1 << 16, 0, -1.0, 1.0)
+    assert np.array_equal(a, b)
+    prod = hg.host_init_random(1 << 16, 0, -1.0, 1.0).numpy()
+    assert np.array_equal(a, prod)
+    vals = oracle.decode_table()[a]
+    assert abs(vals.mean() + 1.0) < 0.02 and abs(vals.std() - 1.0) < 0.02
+
+
+def test_quantiser_matches_product_and_spec():
+    import hipgemm_b200 as hg
+    q, s = oracle.make_quantized((256, 512), 11)
+    qp, sp = hg.host_make_quantized(256 * 512, 11)
+    assert s == sp and np.array_equal(q.ravel(), qp.numpy())
+    x = oracle.normal_f32(256 * 512, 11)
+    assert s == np.float32(np.abs(x).max()) / np.float32(448.0)
+    assert np.abs(oracle.decode_table()[q]).max() == 448.0  # the amax element lands on 448
+
+
+# ---- GEMM ------------------------------------------------------------------------------------
+
+def _numpy_sequential(A, B, sa, sb):
+    """Independent restatement: fp32 accumulator per element, k ascending."""
+    T = oracle.decode_table()
+    a = T[A].astype(np.float32)
+    b = T[B].astype(np.float32)
+    acc = np.zeros((A.shape[0], B.shape[0]), dtype=np.float32)
+    for k in range(A.shape[1]):
+        acc += np.outer(a[:, k], b[:, k]).astype(np.float32)
+    s = np.float32(np.float32(sa) * np.float32(sb))
+    return oracle.bf16_rne_array((s * acc).astype(np.float32))
+
+
+@pytest.mark.parametrize("M,N,K", [(1, 1, 16), (5, 33, 64), (64, 48, 256), (130, 70, 512)])
+def test_gemm_matches_numpy_restatement(M, N, K):
+    A, sa = oracle.make_quantized((M, K), M)
+    B, sb = oracle.make_quantized((N, K), N + 1)
+    assert np.array_equal(oracle.gemm(A, B, sa, sb), _numpy_sequential(A, B, sa, sb))
+
+
+def test_gemm_variants_agree():
+    """Blocked (tests), naive loop nest (timed baseline) and row-list paths: same bits."""
+    A, sa = oracle.make_quantized((96, 256), 1)
+    B, sb = oracle.make_quantized((80, 256), 2)
+    full = oracle.gemm(A, B, sa, sb)
+    assert np.array_equal(oracle.gemm_naive_rows(A, B, 0, 96, sa, sb), full)
+    assert np.array_equal(oracle.gemm_naive_rows(A, B, 10, 37, sa, sb), full[10:37])
+    rows = [0, 5, 95, 40]
+    assert np.array_equal(oracle.gemm_rows(A, B, rows, sa, sb), full[rows])
+    assert np.array_equal(oracle.gemm(A, B, sa, sb, nthreads=1), full)
+
+
+@pytest.mark.parametrize("path", GOLDEN, ids=[os.path.basename(p) for p in GOLDEN])
+def test_oracle_reproduces_golden_fixture(path):
+    g = np.load(path)
+    C = oracle.gemm(g["A"], g["B"], float(g["scale_a"]), float(g["scale_b"]))
+    assert np.array_equal(C, g["C"])
+
+
+def test_golden_fixtures_present():
+    names = {os.path.basename(p) for p in GOLDEN}
+    assert {"tiny_scaled.npz", "reference_mode.npz", "long_k_scaled.npz"} <= names
+
+
+# ---- validator ---------------------------------------------------------------------------------
+
+def test_validator_symmetric_tolerance():
+    ref = oracle.bf16_rne_array(np.array([100.0, -100.0, 0.0, 1e-4], dtype=np.float32))
+    ok = oracle.bf16_rne_array(np.array([100.9, -100.9, 0.0009, -0.0008], dtype=np.float32))
+    bad = oracle.bf16_rne_array(np.array([102.0, -98.0, 0.002, 0.0], dtype=np.float32))
+    assert oracle.validate(ok, ref) == (0, -1)
+    n, first = oracle.validate(bad, ref)
+    assert n == 3 and first == 0
+
+
+def test_reference_validator_signed_threshold_bug():
+    """test.cpp:39 compares diff > c_ref*0.01 without abs(): identical matrices with a
+    negative entry fail it.  The reference's inputs (N(-1,1), test.cpp:70-71) make every
+    C positive, which hides this; the oracle's validate() uses |ref|."""
+    C = oracle.bf16_rne_array(np.array([[1.0, -2.0]], dtype=np.float32))
+    assert not oracle.validate_reference(C, C)
+    assert oracle.validate(C, C)[0] == 0
+    P = oracle.bf16_rne_array(np.array([[1.0, 2.0]], dtype=np.float32))
+    assert oracle.validate_reference(P, P)

@@ -32,13 +32,13 @@ if ROOT not in sys.path:
 
 WORKLOADS = {
     # name: (M, N, K, stddev of B)  -- A is always N(0, 1)
-    "8192": (8192, 8192, 8192, 1.0),          # headline config
-    "4096": (4096, 4096, 4096, 1.0),          # configs[1]
-    "ffn": (16384, 28672, 8192, 0.02),        # configs[3]
-    "skinny128": (128, 8192, 8192, 1.0),      # configs[4]
+    "8192": (8192, 8192, 8192, 1.0),          # headline config (the benchmark metric is quoted on it)
+    "4096": (4096, 4096, 4096, 1.0),          # square single-GPU config
+    "ffn": (16384, 28672, 8192, 0.02),        # LLM-FFN-shaped config
+    "skinny128": (128, 8192, 8192, 1.0),      # skinny / irregular sweep
     "1024x7168x2048": (1024, 7168, 2048, 1.0),
     "4000x5120x7168": (4000, 5120, 7168, 1.0),
-    "512": (512, 512, 512, 1.0),              # configs[0] (the CPU-runnable case)
+    "512": (512, 512, 512, 1.0),              # the CPU-runnable case
 }
 L2_BYTES = 126 * 2**20
 METRIC = "FP8 e4m3 GEMM TFLOP/s and % of dense FP8 peak"
@@ -46,7 +46,7 @@ METRIC = "FP8 e4m3 GEMM TFLOP/s and % of dense FP8 peak"
 # DRAM bytes (read + write) of one launch of the GEMM kernel, from an ncu capture of
 # the same workload (see profiles/); keyed by (workload, gpus).  None = not captured.
 TRAFFIC_BYTES_PER_LAUNCH: dict[tuple[str, int], float] = {
-    ("8192", 1): 336.159e6 + 114.371e6,  # profiles/fp8_gemm_tn_8192_bn256_1cta.md
+    ("8192", 1): 344.333e6 + 116.975e6,  # profiles/fp8_gemm_tn_8192_pair256.md (pair<256, 6>)
 }
 
 

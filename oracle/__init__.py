@@ -42,7 +42,7 @@ _SIG = {
     "oracle_mt19937_nth": (ctypes.c_uint32, [ctypes.c_uint32, ctypes.c_uint64]),
 }
 
-RTOL = 1e-2  # BASELINE tolerance: |c - ref| <= RTOL*|ref| + ATOL per element
+RTOL = 1e-2  # benchmark-config tolerance: |c - ref| <= RTOL*|ref| + ATOL per element
 ATOL = 1e-3
 
 

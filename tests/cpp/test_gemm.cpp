@@ -9,7 +9,7 @@
 //                                    the reference's own inputs: seed 0 for A and B,
 //                                    N(-1, 1) cast straight to e4m3, no scale, launched
 //                                    through fp8_gemm_4wave_256x256x128<M, N, K>(...)
-//   ./test_gemm M N K scaled         runtime shape, BASELINE inputs: A seed 0, B seed 1,
+//   ./test_gemm M N K scaled         runtime shape, benchmark-config inputs: A seed 0, B seed 1,
 //                                    N(0, 1), per-tensor amax/448 scales (hgemm_fp8_tn)
 #include <cuda_runtime.h>
 

@@ -11,7 +11,7 @@ import oracle
 
 def make_inputs(M: int, N: int, K: int, seed_a: int = 0, seed_b: int = 1, mean_a: float = 0.0, std_a: float = 1.0,
                 mean_b: float = 0.0, std_b: float = 1.0, scaled: bool = True):
-    """e4m3 A (MxK), B (NxK) and their scales, BASELINE style (amax/448 per tensor) or,
+    """e4m3 A (MxK), B (NxK) and their scales, benchmark-config style (amax/448 per tensor) or,
     with scaled=False, the reference's raw cast of utils.hpp:27-33 (scale 1)."""
     if scaled:
         A, sa = oracle.make_quantized((M, K), seed_a, mean_a, std_a)

@@ -164,9 +164,11 @@ def cpu_reference_rate(M: int, N: int, K: int, std_b: float, seed: int, budget_s
     rows_avail = min(M, 4096)
     A, sa = oracle.make_quantized((rows_avail, K), seed)
     B, sb = oracle.make_quantized((Ns, K), seed + 1, 0.0, std_b)
-    threads = oracle.max_threads()
+    # Every host core this process may run on, whatever OMP_NUM_THREADS says (torchrun
+    # sets it to 1 per rank).
+    threads = len(os.sched_getaffinity(0)) if hasattr(os, "sched_getaffinity") else (os.cpu_count() or 1)
     t0 = time.perf_counter()
-    oracle.gemm_naive_rows(A, B, 0, 1, sa, sb)
+    oracle.gemm_naive_rows(A, B, 0, 1, sa, sb, nthreads=threads)
     t_row = max(time.perf_counter() - t0, 1e-6)
     per_step = budget_s / max(1, steps + warmup)
     S = int(max(1, min(rows_avail, per_step / t_row)))
@@ -174,7 +176,7 @@ def cpu_reference_rate(M: int, N: int, K: int, std_b: float, seed: int, budget_s
     for i in range(warmup + steps):
         r0 = (i * S) % max(1, rows_avail - S + 1)
         t0 = time.perf_counter()
-        oracle.gemm_naive_rows(A, B, r0, r0 + S, sa, sb)
+        oracle.gemm_naive_rows(A, B, r0, r0 + S, sa, sb, nthreads=threads)
         dt = time.perf_counter() - t0
         if i >= warmup:
             times.append(dt)

@@ -6,12 +6,14 @@ callers that hold their buffers in torch tensors, and adds the M-sharded
 multi-GPU driver (shard.py).
 """
 from ._lib import (HGEMM_ERR_ALIGNMENT, HGEMM_ERR_CUDA, HGEMM_ERR_DEVICE_TIMEOUT, HGEMM_ERR_INVALID_VALUE,
-                   HGEMM_ERR_NO_DEVICE, HGEMM_ERR_UNSUPPORTED, HGEMM_OK, LIB_PATH, HgemmError, check, config_names,
+                   HGEMM_ERR_NO_DEVICE, HGEMM_ERR_UNSUPPORTED, HGEMM_OK, HGEMM_SCHEDULE_AUTO,
+                   HGEMM_SCHEDULE_DATA_PARALLEL, HGEMM_SCHEDULE_STREAM_K, LIB_PATH, HgemmError, check, config_names,
                    lib)
-from .gemm import device_status, fp8_gemm_tn, fp8_gemm_tn_rows, host_init_random, host_make_quantized
+from .gemm import device_status, fp8_gemm_tn, fp8_gemm_tn_rows, host_init_random, host_make_quantized, plan
 
 __all__ = [
     "HGEMM_OK", "HGEMM_ERR_INVALID_VALUE", "HGEMM_ERR_ALIGNMENT", "HGEMM_ERR_UNSUPPORTED", "HGEMM_ERR_CUDA",
-    "HGEMM_ERR_NO_DEVICE", "HGEMM_ERR_DEVICE_TIMEOUT", "LIB_PATH", "HgemmError", "check", "config_names", "lib",
-    "device_status", "fp8_gemm_tn", "fp8_gemm_tn_rows", "host_init_random", "host_make_quantized",
+    "HGEMM_ERR_NO_DEVICE", "HGEMM_ERR_DEVICE_TIMEOUT", "HGEMM_SCHEDULE_AUTO", "HGEMM_SCHEDULE_DATA_PARALLEL",
+    "HGEMM_SCHEDULE_STREAM_K", "LIB_PATH", "HgemmError", "check", "config_names", "lib",
+    "device_status", "fp8_gemm_tn", "fp8_gemm_tn_rows", "host_init_random", "host_make_quantized", "plan",
 ]

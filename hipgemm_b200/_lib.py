@@ -18,6 +18,10 @@ HGEMM_ERR_CUDA = -4
 HGEMM_ERR_NO_DEVICE = -5
 HGEMM_ERR_DEVICE_TIMEOUT = -6
 
+HGEMM_SCHEDULE_AUTO = 0
+HGEMM_SCHEDULE_DATA_PARALLEL = 1
+HGEMM_SCHEDULE_STREAM_K = 2
+
 
 class HgemmError(RuntimeError):
     """A negative status code from the C ABI (never a silent fallback)."""
@@ -36,6 +40,11 @@ _SIGNATURES = {
     "hgemm_fp8_tn": (_i, [_vp, _vp, _vp, _i, _i, _i, _vp, _vp, _vp]),
     "hgemm_fp8_tn_rows": (_i, [_vp, _vp, _vp, _i, _i, _i, _i, _i, _vp, _vp, _vp]),
     "hgemm_fp8_tn_config": (_i, [_vp, _vp, _vp, _i, _i, _i, _vp, _vp, _vp, _i]),
+    "hgemm_fp8_tn_ex": (_i, [_vp, _vp, _vp, _i, _i, _i, _vp, _vp, _vp, _i, _i, _vp, ctypes.c_size_t]),
+    "hgemm_workspace_bytes": (_i, [_i, _i, _i, _i, _i, ctypes.POINTER(ctypes.c_size_t)]),
+    "hgemm_plan": (_i, [_i, _i, _i, _i, _i, ctypes.POINTER(ctypes.c_int)]),
+    "hgemm_debug_schedule": (_i, [ctypes.c_longlong, _i, _i, _i, ctypes.POINTER(ctypes.c_int)]),
+    "hgemm_debug_work_items": (_i, [_i, _i, _i, _i, _i, _i, ctypes.POINTER(ctypes.c_int), _i]),
     "hgemm_num_configs": (_i, []),
     "hgemm_config_resident_ctas": (_i, [_i]),
     "hgemm_config_name": (ctypes.c_char_p, [_i]),

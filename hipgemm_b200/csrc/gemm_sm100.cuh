@@ -6,17 +6,36 @@
 // N x K, C row-major M x N), but built the Blackwell way:
 //   * TMA 2-D tiled loads with 128-byte swizzle into a STAGES-deep shared-memory ring
 //     (replaces buffer_load...lds + the XOR swizzle of fp8_4wave.hpp:80-177);
-//   * one warp issues tcgen05.mma kind::f8f6f4 (M=128, N=BN, K=32) accumulating in
+//   * one thread issues tcgen05.mma kind::f8f6f4 (K=32 per instruction) accumulating in
 //     tensor memory (replaces the 16x16x128 MFMA register tiles, :24-74, and the
 //     LDS->VGPR fragment loads, :179-212);
 //   * warp specialisation with mbarrier hand-off (producer / MMA / 4 epilogue warps)
 //     instead of the hand-interleaved 4-wave schedule (:244-332, :428-463);
 //   * a persistent grid walks output tiles in GROUP_M-grouped raster order, the
-//     analogue of the reference's WGM=4 L2 swizzle (:357-377);
+//     analogue of the reference's WGM=4 L2 swizzle (:357-377), and splits the last
+//     one-to-two waves of tiles along K across all slots ("stream-K") so short or
+//     wave-quantised problems keep every SM busy;
 //   * two accumulator buffers in tensor memory so the epilogue of tile i overlaps the
 //     MMAs of tile i+1; the epilogue scales, rounds to bf16 (RNE, where the reference
 //     truncates, :214-217) and writes through shared memory with TMA stores, which clip
 //     ragged M/N edges (the reference requires M%256 == N%256 == 0 and K%128 == 0).
+//
+// One kernel template covers two shapes of the work:
+//   CTAS = 1: one CTA computes a 128 x BN tile with M=128 MMAs;
+//   CTAS = 2: a cluster of two CTAs on two SMs computes a 256 x BN tile with M=256
+//             MMAs (cta_group::2) issued by the even CTA.  Each CTA stages its own 128
+//             rows of A and BN/2 rows of B per K block, so per-SM operand traffic per
+//             MAC is a third lower than the 128 x 256 single-CTA tile; each CTA's tensor
+//             memory holds its 128 accumulator rows and each CTA runs its own epilogue.
+//
+// CTA-pair synchronisation uses no multicast form: tcgen05.commit always targets a
+// barrier of the even CTA, and the even CTA forwards each completion to its peer with a
+// remote mbarrier.arrive that the peer acquires at cluster scope:
+//   full[s]    even CTA only; expects both CTAs' TMA bytes (the odd CTA's loads name the
+//              even CTA's barrier through mapa and the cta_group::2 TMA form);
+//   empty[s]   even: MMA commit; odd: forwarded by the even producer after its own wait;
+//   tfull[a]   even: MMA commit; odd: forwarded by the even CTA's first epilogue warp;
+//   tempty[a]  even CTA only; one arrive per epilogue warp of both CTAs (count 8).
 #pragma once
 
 #include <cuda.h>
@@ -29,9 +48,19 @@ namespace hg {
 struct GemmParams {
     int M, N, K;
     int num_m_blocks, num_n_blocks, num_k_blocks;
-    int group_m;  // tile rows per raster group
+    int group_m;           // tile rows per raster group
     const float* scale_a;  // device pointers, nullptr = 1.0
     const float* scale_b;
+    // Hybrid schedule.  The first dp_tiles tiles (raster order) are whole-tile items dealt
+    // round-robin to the slots (CTAs, or CTA pairs).  The last sk_tiles tiles are cut into
+    // k-block units; slot s < sk_slots owns units [sk_begin(s), sk_begin(s + 1)).  A tile
+    // shared by several slots is reduced by whichever contributor finishes last: each one
+    // writes its fp32 partial to `partials`, then bumps the tile's counter.
+    int dp_tiles;
+    int sk_tiles;
+    int sk_slots;
+    float* partials;  // [slot][piece 0/1][cta][128 x BN] fp32 (layout: partial_offset)
+    int* counters;    // [sk tile][cta]; zero on entry, left zero on exit
 };
 
 // Status codes recorded by an expired bounded wait: role << 8 | site.
@@ -46,46 +75,155 @@ enum : uint32_t {
 // Output tile -> (m block, n block) with GROUP_M tile rows per raster group: inside a
 // group the walk goes down the rows first, then across the columns, so the CTAs that
 // run at the same time share both A row panels and B column panels in L2.
-__device__ __forceinline__ void tile_coords(int tile, const GemmParams& p, int& mb, int& nb) {
+__host__ __device__ __forceinline__ void tile_coords(int tile, const GemmParams& p, int& mb, int& nb) {
     const int per_group = p.group_m * p.num_n_blocks;
     const int group = tile / per_group;
     const int first_m = group * p.group_m;
-    const int rows_in_group = min(p.num_m_blocks - first_m, p.group_m);
+    const int rows_in_group = p.num_m_blocks - first_m < p.group_m ? p.num_m_blocks - first_m : p.group_m;
     const int r = tile - group * per_group;
     mb = first_m + r % rows_in_group;
     nb = r / rows_in_group;
 }
 
-template <int BN, int STAGES>
-struct GemmConfig {
-    static constexpr int BM = 128;
-    static constexpr int BK = 128;  // bytes of K per stage = one 128-byte swizzle row
+struct Work {
+    int tile;      // raster tile index
+    int kb_begin;  // k blocks [kb_begin, kb_end) of that tile
+    int kb_end;
+    int piece;     // -1: the whole tile (store C directly); 0/1: this slot's first/last partial
+};
+
+__host__ __device__ __forceinline__ long long sk_begin(const GemmParams& p, int s) {
+    return static_cast<long long>(s) * (static_cast<long long>(p.sk_tiles) * p.num_k_blocks) / p.sk_slots;
+}
+
+// Item `idx` (0-based) of slot `slot` out of `nslots`; false once the slot has no more.
+// Every role of a CTA (and both CTAs of a pair) walks the same sequence:
+//   1. this slot's partial stream-K pieces (at most two: the tail of its first tile,
+//      piece 0, and the head of its last tile, piece 1), so that the reductions of
+//      shared tiles run while the MMAs continue with whole tiles;
+//   2. whole tiles of its stream-K range;
+//   3. its data-parallel tiles slot, slot + nslots, ...
+__host__ __device__ __forceinline__ bool get_work(const GemmParams& p, int slot, int nslots, int idx, Work& w) {
+    const int KB = p.num_k_blocks;
+    int n_part = 0, n_full = 0, t_first = 0, t_last = -1;
+    long long u0 = 0, u1 = 0;
+    bool first_partial = false, last_partial = false;
+    if (slot < p.sk_slots) {
+        u0 = sk_begin(p, slot);
+        u1 = sk_begin(p, slot + 1);
+        if (u1 > u0) {
+            t_first = static_cast<int>(u0 / KB);
+            t_last = static_cast<int>((u1 - 1) / KB);
+            const long long first_end = t_first == t_last ? u1 : static_cast<long long>(t_first + 1) * KB;
+            first_partial = u0 != static_cast<long long>(t_first) * KB || first_end != static_cast<long long>(t_first + 1) * KB;
+            last_partial = t_last != t_first && u1 != static_cast<long long>(t_last + 1) * KB;
+            n_part = (first_partial ? 1 : 0) + (last_partial ? 1 : 0);
+            n_full = (t_last - t_first + 1) - n_part;
+        }
+    }
+    if (idx < n_part) {
+        const bool first = first_partial && idx == 0;
+        const int t = first ? t_first : t_last;
+        w.tile = p.dp_tiles + t;
+        w.kb_begin = first ? static_cast<int>(u0 - static_cast<long long>(t) * KB) : 0;
+        w.kb_end = (first && t_first != t_last) ? KB : static_cast<int>(u1 - static_cast<long long>(t) * KB);
+        if (!first) w.kb_end = static_cast<int>(u1 - static_cast<long long>(t) * KB);
+        w.piece = first ? 0 : 1;
+        return true;
+    }
+    idx -= n_part;
+    if (idx < n_full) {
+        w.tile = p.dp_tiles + t_first + (first_partial ? 1 : 0) + idx;
+        w.kb_begin = 0;
+        w.kb_end = KB;
+        w.piece = -1;
+        return true;
+    }
+    idx -= n_full;
+    const int dp_count = p.dp_tiles > slot ? (p.dp_tiles - slot + nslots - 1) / nslots : 0;
+    if (idx < dp_count) {
+        w.tile = slot + idx * nslots;
+        w.kb_begin = 0;
+        w.kb_end = KB;
+        w.piece = -1;
+        return true;
+    }
+    return false;
+}
+
+// The stream-K slot whose unit range contains unit u (u < sk_tiles * num_k_blocks).
+__host__ __device__ __forceinline__ int sk_slot_of_unit(const GemmParams& p, long long u) {
+    const long long U = static_cast<long long>(p.sk_tiles) * p.num_k_blocks;
+    int s = static_cast<int>(u * p.sk_slots / U);
+    while (s + 1 < p.sk_slots && sk_begin(p, s + 1) <= u) ++s;
+    while (s > 0 && sk_begin(p, s) > u) --s;
+    return s;
+}
+
+// Float offset, inside one 128 x BN partial, of columns [32*c32 + 4*j4, +4) of the row
+// that thread (quad, lane) owns.  Lanes are the fastest-varying index, so the 32 lanes
+// of a warp access 512 contiguous bytes for each (c32, j4): full-line transactions.
+template <int BN>
+__device__ __forceinline__ uint32_t partial_offset(uint32_t quad, uint32_t c32, uint32_t j4, uint32_t lane) {
+    return (((quad * (BN / 32) + c32) * 8u + j4) * 32u + lane) * 4u;
+}
+
+__device__ __forceinline__ void named_bar_sync(uint32_t id, uint32_t count) {
+    asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(count) : "memory");
+}
+
+// Barrier over `count` threads that also ANDs a predicate across them.
+__device__ __forceinline__ bool named_bar_all(uint32_t id, uint32_t count, bool pred) {
+    uint32_t r;
+    asm volatile(
+        "{\n\t.reg .pred pi, po;\n\t"
+        "setp.ne.u32 pi, %1, 0;\n\t"
+        "bar.red.and.pred po, %2, %3, pi;\n\t"
+        "selp.u32 %0, 1, 0, po;\n\t}\n"
+        : "=r"(r)
+        : "r"(static_cast<uint32_t>(pred)), "r"(id), "r"(count)
+        : "memory");
+    return r != 0;
+}
+
+__device__ __forceinline__ void st_global_v4(float* p, float a, float b, float c, float d) {
+    asm volatile("st.global.v4.f32 [%0], {%1, %2, %3, %4};" ::"l"(p), "f"(a), "f"(b), "f"(c), "f"(d) : "memory");
+}
+
+template <int CTAS, int BN, int STAGES>
+struct KernelShape {
+    static constexpr int BM = 128 * CTAS;   // output tile rows
+    static constexpr int BK = 128;          // bytes of K per stage = one 128-byte swizzle row
     static constexpr int UMMA_K = 32;
     static constexpr int kNumThreads = 192;  // warp 0 TMA, warp 1 MMA, warps 2-5 epilogue
-    static constexpr int A_BYTES = BM * BK;
-    static constexpr int B_BYTES = BN * BK;
+    static constexpr int B_ROWS = BN / CTAS;  // rows of B this CTA stages per K block
+    static constexpr int A_BYTES = 128 * BK;
+    static constexpr int B_BYTES = B_ROWS * BK;
     static constexpr int STAGE_BYTES = A_BYTES + B_BYTES;
-    static constexpr int EPI_COLS = 64;                 // bf16 columns per staged chunk (128 B)
+    static constexpr int EPI_COLS = 64;                      // bf16 columns per staged chunk (128 B)
     static constexpr int EPI_BUF_BYTES = 32 * EPI_COLS * 2;  // one warp's 32 rows x 128 B
     static constexpr int OFF_A = 0;
     static constexpr int OFF_B = OFF_A + STAGES * A_BYTES;
     static constexpr int OFF_EPI = OFF_B + STAGES * B_BYTES;
     static constexpr int OFF_BAR = OFF_EPI + 4 * 2 * EPI_BUF_BYTES;
-    static constexpr int NUM_BARS = 2 * STAGES + 5;  // full, empty, tmem_full x2, tmem_empty x2, drain
+    static constexpr int NUM_BARS = 2 * STAGES + 5;  // full, empty, tfull x2, tempty x2, drain
     static constexpr int OFF_MISC = OFF_BAR + NUM_BARS * 8;
     static constexpr int SMEM_BYTES = OFF_MISC + 16 + 1024;  // + slack to align the base to 1024 B
     static constexpr uint32_t TMEM_COLS = 2 * BN < 32 ? 32 : 2 * BN;
     static constexpr uint32_t IDESC = idesc_e4m3_f32(BM, BN);
+    static constexpr int PARTIAL_FLOATS = 128 * BN;  // one CTA's share of a partial tile
+    static_assert(CTAS == 1 || CTAS == 2, "one CTA or a CTA pair");
     static_assert(BN % 64 == 0 && BN >= 64 && BN <= 256, "BN must be 64, 128, 192 or 256");
+    static_assert(B_BYTES % 1024 == 0, "B tiles must keep 1024-byte alignment");
     static_assert((TMEM_COLS & (TMEM_COLS - 1)) == 0, "tensor memory allocations are powers of two");
     static_assert(SMEM_BYTES <= 232448, "exceeds 227 KB of shared memory per CTA");
 };
 
-template <int BN, int STAGES>
+template <int CTAS, int BN, int STAGES>
 __global__ void __launch_bounds__(192, 1)
     fp8_gemm_tn_sm100(const __grid_constant__ CUtensorMap tm_a, const __grid_constant__ CUtensorMap tm_b,
                       const __grid_constant__ CUtensorMap tm_c, const GemmParams p) {
-    using Cfg = GemmConfig<BN, STAGES>;
+    using S = KernelShape<CTAS, BN, STAGES>;
     extern __shared__ uint8_t smem_raw[];
     // 128-byte swizzle atoms need 1024-byte alignment.
     const uint32_t raw_base = smem_u32(smem_raw);
@@ -94,262 +232,20 @@ __global__ void __launch_bounds__(192, 1)
 
     const uint32_t warp = threadIdx.x / 32;
     const uint32_t lane = threadIdx.x % 32;
-
-    const uint32_t bar_full = base + Cfg::OFF_BAR;
-    const uint32_t bar_empty = bar_full + STAGES * 8;
-    const uint32_t bar_tfull = bar_empty + STAGES * 8;
-    const uint32_t bar_tempty = bar_tfull + 2 * 8;
-    const uint32_t bar_drain = bar_tempty + 2 * 8;
-    const uint32_t tmem_slot = base + Cfg::OFF_MISC;
-    volatile uint32_t* const tmem_slot_ptr = reinterpret_cast<volatile uint32_t*>(smem_gen + Cfg::OFF_MISC);
-    volatile uint32_t* const abort_flag = reinterpret_cast<volatile uint32_t*>(smem_gen + Cfg::OFF_MISC + 4);
-
-    if (threadIdx.x == 0) {
-        for (int s = 0; s < STAGES; ++s) {
-            mbar_init(bar_full + 8 * s, 1);
-            mbar_init(bar_empty + 8 * s, 1);
-        }
-        for (int a = 0; a < 2; ++a) {
-            mbar_init(bar_tfull + 8 * a, 1);
-            mbar_init(bar_tempty + 8 * a, 128);
-        }
-        mbar_init(bar_drain, 1);
-        *abort_flag = 0u;
-        fence_mbarrier_init();
-        fence_proxy_async_smem();
-        prefetch_tmap(&tm_a);
-        prefetch_tmap(&tm_b);
-        prefetch_tmap(&tm_c);
-    }
-    if (warp == 1) {
-        tmem_alloc<1>(tmem_slot, Cfg::TMEM_COLS);
-        tmem_relinquish<1>();
-    }
-    tc_fence_before();
-    __syncthreads();
-    tc_fence_after();
-    const uint32_t tmem_base = *tmem_slot_ptr;
-
-    const int num_tiles = p.num_m_blocks * p.num_n_blocks;
-
-    if (warp == 0) {
-        // ---------------- TMA producer ----------------
-        if (lane == 0) {
-            int stage = 0;
-            uint32_t phase = 0;
-            bool ok = true;
-            for (int tile = blockIdx.x; tile < num_tiles && ok; tile += gridDim.x) {
-                int mb, nb;
-                tile_coords(tile, p, mb, nb);
-                for (int kb = 0; kb < p.num_k_blocks; ++kb) {
-                    if (!mbar_wait(bar_empty + 8 * stage, phase ^ 1u, abort_flag, kErrProducerEmpty)) {
-                        ok = false;
-                        break;
-                    }
-                    const uint32_t full = bar_full + 8 * stage;
-                    mbar_arrive_expect_tx(full, Cfg::STAGE_BYTES);
-                    tma_load_2d(base + Cfg::OFF_A + stage * Cfg::A_BYTES, &tm_a, kb * Cfg::BK, mb * Cfg::BM, full);
-                    tma_load_2d(base + Cfg::OFF_B + stage * Cfg::B_BYTES, &tm_b, kb * Cfg::BK, nb * BN, full);
-                    if (++stage == STAGES) {
-                        stage = 0;
-                        phase ^= 1u;
-                    }
-                }
-            }
-            // On abort, give copies already in flight time to land before the CTA exits.
-            if (!ok) sleep_ns_bounded(1000000);
-        }
-    } else if (warp == 1) {
-        // ---------------- MMA issuer (one thread) ----------------
-        if (lane == 0) {
-            int stage = 0;
-            uint32_t phase = 0;
-            int acc = 0;
-            uint32_t acc_phase = 0;
-            bool ok = true;
-            for (int tile = blockIdx.x; tile < num_tiles && ok; tile += gridDim.x) {
-                if (!mbar_wait(bar_tempty + 8 * acc, acc_phase ^ 1u, abort_flag, kErrMmaTmemEmpty)) {
-                    ok = false;
-                    break;
-                }
-                tc_fence_after();
-                const uint32_t d_tmem = tmem_base + static_cast<uint32_t>(acc * BN);
-                for (int kb = 0; kb < p.num_k_blocks; ++kb) {
-                    if (!mbar_wait(bar_full + 8 * stage, phase, abort_flag, kErrMmaFull)) {
-                        ok = false;
-                        break;
-                    }
-                    tc_fence_after();
-                    const uint64_t a_desc = sw128_kmajor_desc(base + Cfg::OFF_A + stage * Cfg::A_BYTES);
-                    const uint64_t b_desc = sw128_kmajor_desc(base + Cfg::OFF_B + stage * Cfg::B_BYTES);
-#pragma unroll
-                    for (int k = 0; k < Cfg::BK / Cfg::UMMA_K; ++k) {
-                        // Advancing the start address by 32 B walks K inside the swizzle
-                        // atom: the hardware applies the XOR pattern to the final address.
-                        const uint64_t koff = static_cast<uint64_t>((k * Cfg::UMMA_K) >> 4);
-                        mma_f8f6f4<1>(d_tmem, a_desc + koff, b_desc + koff, Cfg::IDESC, (kb | k) != 0 ? 1u : 0u);
-                    }
-                    mma_commit<1>(bar_empty + 8 * stage);  // frees the stage when these MMAs finish
-                    if (++stage == STAGES) {
-                        stage = 0;
-                        phase ^= 1u;
-                    }
-                }
-                if (!ok) break;
-                mma_commit<1>(bar_tfull + 8 * acc);  // accumulator ready for the epilogue
-                if (++acc == 2) {
-                    acc = 0;
-                    acc_phase ^= 1u;
-                }
-            }
-            if (!ok) {
-                // Let MMAs already issued finish before tensor memory is released.
-                mma_commit<1>(bar_drain);
-                volatile uint32_t never = 0;
-                mbar_wait(bar_drain, 0, &never, kErrMmaDrain);
-            }
-        }
-    } else {
-        // ---------------- epilogue: 4 warps, TMEM -> regs -> smem -> TMA store ----------------
-        const uint32_t quad = warp % 4;  // tensor-memory lanes [32*quad, 32*quad + 32)
-        const uint32_t epi_idx = warp - 2;
-        const float sa = p.scale_a ? *p.scale_a : 1.0f;
-        const float sb = p.scale_b ? *p.scale_b : 1.0f;
-        const float s = sa * sb;
-        const uint32_t stage_base = base + Cfg::OFF_EPI + epi_idx * 2 * Cfg::EPI_BUF_BYTES;
-        int acc = 0;
-        uint32_t acc_phase = 0;
-        uint32_t chunk_ctr = 0;
-        for (int tile = blockIdx.x; tile < num_tiles; tile += gridDim.x) {
-            int mb, nb;
-            tile_coords(tile, p, mb, nb);
-            // Warp-uniform decision: the tcgen05.ld below is .sync.aligned.
-            const bool ready = mbar_wait(bar_tfull + 8 * acc, acc_phase, abort_flag, kErrEpiTmemFull);
-            if (!__all_sync(0xffffffffu, ready)) break;
-            tc_fence_after();
-            const int row0 = mb * Cfg::BM + static_cast<int>(quad) * 32;
-#pragma unroll 1
-            for (int c = 0; c < BN / Cfg::EPI_COLS; ++c) {
-                uint32_t v[64];
-                const uint32_t taddr = tmem_base + ((quad * 32u) << 16) + static_cast<uint32_t>(acc * BN + c * 64);
-                tmem_ld_32x32b_x32(taddr, *reinterpret_cast<uint32_t(*)[32]>(&v[0]));
-                tmem_ld_32x32b_x32(taddr + 32, *reinterpret_cast<uint32_t(*)[32]>(&v[32]));
-                tmem_ld_wait();
-                uint32_t packed[32];
-#pragma unroll
-                for (int j = 0; j < 32; ++j) {
-                    packed[j] = pack_bf16x2_rn(__fmul_rn(__uint_as_float(v[2 * j]), s),
-                                               __fmul_rn(__uint_as_float(v[2 * j + 1]), s));
-                }
-                const uint32_t buf = chunk_ctr & 1u;
-                // The store issued two chunks ago read this buffer; wait until it has.
-                if (lane == 0) bulk_wait_group_read<1>();
-                __syncwarp();
-                const uint32_t row_addr = stage_base + buf * Cfg::EPI_BUF_BYTES + lane * 128u;
-#pragma unroll
-                for (int q = 0; q < 8; ++q) {
-                    const uint32_t slot = static_cast<uint32_t>(q) ^ (lane & 7u);  // 128-byte swizzle
-                    st_shared_v4(row_addr + slot * 16u, packed[4 * q], packed[4 * q + 1], packed[4 * q + 2],
-                                 packed[4 * q + 3]);
-                }
-                fence_proxy_async_smem();
-                __syncwarp();
-                if (lane == 0) {
-                    const int col0 = nb * BN + c * Cfg::EPI_COLS;
-                    if (row0 < p.M && col0 < p.N) {
-                        tma_store_2d(&tm_c, col0, row0, stage_base + buf * Cfg::EPI_BUF_BYTES);
-                    }
-                    bulk_commit_group();
-                }
-                ++chunk_ctr;
-            }
-            tc_fence_before();
-            mbar_arrive(bar_tempty + 8 * acc);
-            if (++acc == 2) {
-                acc = 0;
-                acc_phase ^= 1u;
-            }
-        }
-        if (lane == 0) bulk_wait_group<0>();
-        __syncwarp();
-    }
-
-    tc_fence_before();
-    __syncthreads();
-    if (warp == 1) {
-        tc_fence_after();
-        tmem_dealloc<1>(tmem_base, Cfg::TMEM_COLS);
-    }
-}
-
-
-// ======================================================================================
-// CTA-pair variant (cta_group::2): a cluster of two CTAs on two SMs computes one
-// 256 x BN output tile with M=256 tcgen05.mma instructions issued by the even CTA.
-// Each CTA stages its own half of A (128 rows) and its own half of B (BN/2 rows) per
-// K block, so per-SM operand traffic per MAC is a third lower than the 128 x 256
-// single-CTA tile (32 KB instead of 48 KB per 4 M MACs per SM); each CTA's tensor
-// memory receives its 128 rows of the accumulator and each CTA runs its own epilogue.
-//
-// Synchronisation without any multicast form: tcgen05.commit always targets a barrier
-// of the issuing (even) CTA, and the even CTA forwards each completion to its peer with
-// a remote mbarrier.arrive (release.cluster) that the peer acquires at cluster scope:
-//   full[s]    even CTA only; expects both CTAs' TMA bytes (the odd CTA's loads name
-//              the even CTA's barrier through mapa and the cta_group::2 TMA form);
-//   empty[s]   even: MMA commit; odd: forwarded by the even producer after its own wait;
-//   tfull[a]   even: MMA commit; odd: forwarded by the even CTA's first epilogue warp;
-//   tempty[a]  even CTA only; one arrive per epilogue warp of both CTAs (count 8).
-// ======================================================================================
-
-template <int BN, int STAGES>
-struct PairConfig {
-    static constexpr int BM = 256;       // pair tile rows (128 per CTA)
-    static constexpr int BK = 128;
-    static constexpr int UMMA_K = 32;
-    static constexpr int kNumThreads = 192;
-    static constexpr int A_BYTES = 128 * BK;        // this CTA's half of A
-    static constexpr int B_BYTES = (BN / 2) * BK;   // this CTA's half of B
-    static constexpr int STAGE_BYTES = A_BYTES + B_BYTES;
-    static constexpr int EPI_COLS = 64;
-    static constexpr int EPI_BUF_BYTES = 32 * EPI_COLS * 2;
-    static constexpr int OFF_A = 0;
-    static constexpr int OFF_B = OFF_A + STAGES * A_BYTES;
-    static constexpr int OFF_EPI = OFF_B + STAGES * B_BYTES;
-    static constexpr int OFF_BAR = OFF_EPI + 4 * 2 * EPI_BUF_BYTES;
-    static constexpr int NUM_BARS = 2 * STAGES + 5;
-    static constexpr int OFF_MISC = OFF_BAR + NUM_BARS * 8;
-    static constexpr int SMEM_BYTES = OFF_MISC + 16 + 1024;
-    static constexpr uint32_t TMEM_COLS = 2 * BN;
-    static constexpr uint32_t IDESC = idesc_e4m3_f32(BM, BN);
-    static_assert(BN == 128 || BN == 256, "pair tiles are 256 x 128 or 256 x 256");
-    static_assert(((BN / 2) * BK) % 1024 == 0, "B half-tile must keep 1024-byte alignment");
-    static_assert(SMEM_BYTES <= 232448, "exceeds 227 KB of shared memory per CTA");
-};
-
-template <int BN, int STAGES>
-__global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(192, 1)
-    fp8_gemm_tn_sm100_pair(const __grid_constant__ CUtensorMap tm_a, const __grid_constant__ CUtensorMap tm_b,
-                           const __grid_constant__ CUtensorMap tm_c, const GemmParams p) {
-    using Cfg = PairConfig<BN, STAGES>;
-    extern __shared__ uint8_t smem_raw[];
-    const uint32_t raw_base = smem_u32(smem_raw);
-    const uint32_t base = (raw_base + 1023u) & ~1023u;
-    uint8_t* const smem_gen = smem_raw + (base - raw_base);
-
-    const uint32_t warp = threadIdx.x / 32;
-    const uint32_t lane = threadIdx.x % 32;
-    const uint32_t rank = cluster_ctarank();  // 0 = even CTA (issues the MMAs), 1 = odd
+    const uint32_t rank = CTAS == 2 ? cluster_ctarank() : 0u;  // 0 issues the MMAs
     const uint32_t peer = rank ^ 1u;
     const bool leader = rank == 0;
+    constexpr bool kPair = CTAS == 2;
 
-    const uint32_t bar_full = base + Cfg::OFF_BAR;
+    const uint32_t bar_full = base + S::OFF_BAR;
     const uint32_t bar_empty = bar_full + STAGES * 8;
     const uint32_t bar_tfull = bar_empty + STAGES * 8;
     const uint32_t bar_tempty = bar_tfull + 2 * 8;
     const uint32_t bar_drain = bar_tempty + 2 * 8;
-    const uint32_t tmem_slot = base + Cfg::OFF_MISC;
-    volatile uint32_t* const tmem_slot_ptr = reinterpret_cast<volatile uint32_t*>(smem_gen + Cfg::OFF_MISC);
-    volatile uint32_t* const abort_flag = reinterpret_cast<volatile uint32_t*>(smem_gen + Cfg::OFF_MISC + 4);
+    const uint32_t tmem_slot = base + S::OFF_MISC;
+    volatile uint32_t* const tmem_slot_ptr = reinterpret_cast<volatile uint32_t*>(smem_gen + S::OFF_MISC);
+    volatile uint32_t* const abort_flag = reinterpret_cast<volatile uint32_t*>(smem_gen + S::OFF_MISC + 4);
+    volatile int* const bcast = reinterpret_cast<volatile int*>(smem_gen + S::OFF_MISC + 8);
 
     if (threadIdx.x == 0) {
         for (int s = 0; s < STAGES; ++s) {
@@ -358,7 +254,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(192, 1)
         }
         for (int a = 0; a < 2; ++a) {
             mbar_init(bar_tfull + 8 * a, 1);
-            mbar_init(bar_tempty + 8 * a, 8);
+            mbar_init(bar_tempty + 8 * a, kPair ? 8 : 4);  // one arrive per epilogue warp
         }
         mbar_init(bar_drain, 1);
         *abort_flag = 0u;
@@ -369,50 +265,54 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(192, 1)
         prefetch_tmap(&tm_c);
     }
     if (warp == 1) {
-        tmem_alloc<2>(tmem_slot, Cfg::TMEM_COLS);  // collective with the peer's warp 1
-        tmem_relinquish<2>();
+        tmem_alloc<CTAS>(tmem_slot, S::TMEM_COLS);  // for a pair: collective with the peer's warp 1
+        tmem_relinquish<CTAS>();
     }
     tc_fence_before();
-    cluster_sync();  // barriers of both CTAs initialised, tensor memory allocated
+    if constexpr (kPair) {
+        cluster_sync();  // both CTAs' barriers initialised, tensor memory allocated
+    } else {
+        __syncthreads();
+    }
     tc_fence_after();
     const uint32_t tmem_base = *tmem_slot_ptr;
 
-    const int num_tiles = p.num_m_blocks * p.num_n_blocks;
-    const int pair_id = static_cast<int>(blockIdx.x >> 1);
-    const int num_pairs = static_cast<int>(gridDim.x >> 1);
+    const int slot = static_cast<int>(blockIdx.x) / CTAS;
+    const int nslots = static_cast<int>(gridDim.x) / CTAS;
 
     if (warp == 0) {
-        // ---------------- TMA producer (both CTAs) ----------------
+        // ---------------- TMA producer (one thread per CTA) ----------------
         if (lane == 0) {
-            const uint32_t full_leader0 = mapa_shared(bar_full, 0);
-            const uint32_t peer_empty0 = mapa_shared(bar_empty, peer);
+            const uint32_t full_leader0 = kPair ? mapa_shared(bar_full, 0) : bar_full;
+            const uint32_t peer_empty0 = kPair ? mapa_shared(bar_empty, peer) : 0u;
             int stage = 0;
             uint32_t phase = 0;
             bool first_pass = true;
             bool ok = true;
-            for (int tile = pair_id; tile < num_tiles && ok; tile += num_pairs) {
+            Work w;
+            for (int idx = 0; ok && get_work(p, slot, nslots, idx, w); ++idx) {
                 int mb, nb;
-                tile_coords(tile, p, mb, nb);
-                const int a_row = mb * Cfg::BM + static_cast<int>(rank) * 128;
-                const int b_row = nb * BN + static_cast<int>(rank) * (BN / 2);
-                for (int kb = 0; kb < p.num_k_blocks; ++kb) {
-                    if (!mbar_wait<true>(bar_empty + 8 * stage, phase ^ 1u, abort_flag, kErrProducerEmpty)) {
+                tile_coords(w.tile, p, mb, nb);
+                const int a_row = mb * S::BM + static_cast<int>(rank) * 128;
+                const int b_row = nb * BN + static_cast<int>(rank) * S::B_ROWS;
+                for (int kb = w.kb_begin; kb < w.kb_end; ++kb) {
+                    if (!mbar_wait<kPair>(bar_empty + 8 * stage, phase ^ 1u, abort_flag, kErrProducerEmpty)) {
                         ok = false;
                         break;
                     }
-                    const uint32_t a_dst = base + Cfg::OFF_A + stage * Cfg::A_BYTES;
-                    const uint32_t b_dst = base + Cfg::OFF_B + stage * Cfg::B_BYTES;
+                    const uint32_t a_dst = base + S::OFF_A + stage * S::A_BYTES;
+                    const uint32_t b_dst = base + S::OFF_B + stage * S::B_BYTES;
                     if (leader) {
-                        // The MMAs that read this stage have finished in both CTAs: tell the peer.
-                        if (!first_pass) mbar_arrive_cluster(peer_empty0 + 8 * stage);
+                        // For a pair: the MMAs that read this stage finished in both CTAs.
+                        if (kPair && !first_pass) mbar_arrive_cluster(peer_empty0 + 8 * stage);
                         const uint32_t full = bar_full + 8 * stage;
-                        mbar_arrive_expect_tx(full, 2 * Cfg::STAGE_BYTES);
-                        tma_load_2d(a_dst, &tm_a, kb * Cfg::BK, a_row, full);
-                        tma_load_2d(b_dst, &tm_b, kb * Cfg::BK, b_row, full);
+                        mbar_arrive_expect_tx(full, CTAS * S::STAGE_BYTES);
+                        tma_load_2d(a_dst, &tm_a, kb * S::BK, a_row, full);
+                        tma_load_2d(b_dst, &tm_b, kb * S::BK, b_row, full);
                     } else {
                         const uint32_t full = full_leader0 + 8 * stage;
-                        tma_load_2d_pair(a_dst, &tm_a, kb * Cfg::BK, a_row, full);
-                        tma_load_2d_pair(b_dst, &tm_b, kb * Cfg::BK, b_row, full);
+                        tma_load_2d_pair(a_dst, &tm_a, kb * S::BK, a_row, full);
+                        tma_load_2d_pair(b_dst, &tm_b, kb * S::BK, b_row, full);
                     }
                     if (++stage == STAGES) {
                         stage = 0;
@@ -421,111 +321,106 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(192, 1)
                     }
                 }
             }
+            // On abort, give copies already in flight time to land before the CTA exits.
             if (!ok) sleep_ns_bounded(1000000);
         }
     } else if (warp == 1) {
-        // ---------------- MMA issuer (even CTA, one thread) ----------------
+        // ---------------- MMA issuer (one thread of the even CTA) ----------------
         if (leader && lane == 0) {
             int stage = 0;
             uint32_t phase = 0;
             int acc = 0;
             uint32_t acc_phase = 0;
             bool ok = true;
-            for (int tile = pair_id; tile < num_tiles && ok; tile += num_pairs) {
-                if (!mbar_wait<true>(bar_tempty + 8 * acc, acc_phase ^ 1u, abort_flag, kErrMmaTmemEmpty)) {
+            Work w;
+            for (int idx = 0; ok && get_work(p, slot, nslots, idx, w); ++idx) {
+                if (!mbar_wait<kPair>(bar_tempty + 8 * acc, acc_phase ^ 1u, abort_flag, kErrMmaTmemEmpty)) {
                     ok = false;
                     break;
                 }
                 tc_fence_after();
                 const uint32_t d_tmem = tmem_base + static_cast<uint32_t>(acc * BN);
-                for (int kb = 0; kb < p.num_k_blocks; ++kb) {
-                    if (!mbar_wait<true>(bar_full + 8 * stage, phase, abort_flag, kErrMmaFull)) {
+                for (int kb = w.kb_begin; kb < w.kb_end; ++kb) {
+                    if (!mbar_wait<kPair>(bar_full + 8 * stage, phase, abort_flag, kErrMmaFull)) {
                         ok = false;
                         break;
                     }
                     tc_fence_after();
-                    const uint64_t a_desc = sw128_kmajor_desc(base + Cfg::OFF_A + stage * Cfg::A_BYTES);
-                    const uint64_t b_desc = sw128_kmajor_desc(base + Cfg::OFF_B + stage * Cfg::B_BYTES);
+                    const uint64_t a_desc = sw128_kmajor_desc(base + S::OFF_A + stage * S::A_BYTES);
+                    const uint64_t b_desc = sw128_kmajor_desc(base + S::OFF_B + stage * S::B_BYTES);
 #pragma unroll
-                    for (int k = 0; k < Cfg::BK / Cfg::UMMA_K; ++k) {
-                        const uint64_t koff = static_cast<uint64_t>((k * Cfg::UMMA_K) >> 4);
-                        mma_f8f6f4<2>(d_tmem, a_desc + koff, b_desc + koff, Cfg::IDESC, (kb | k) != 0 ? 1u : 0u);
+                    for (int k = 0; k < S::BK / S::UMMA_K; ++k) {
+                        // Advancing the start address by 32 B walks K inside the swizzle
+                        // atom: the hardware applies the XOR pattern to the final address.
+                        const uint64_t koff = static_cast<uint64_t>((k * S::UMMA_K) >> 4);
+                        const uint32_t accumulate = (kb > w.kb_begin || k > 0) ? 1u : 0u;
+                        mma_f8f6f4<CTAS>(d_tmem, a_desc + koff, b_desc + koff, S::IDESC, accumulate);
                     }
-                    mma_commit<2>(bar_empty + 8 * stage);
+                    mma_commit<CTAS>(bar_empty + 8 * stage);  // frees the stage when these MMAs finish
                     if (++stage == STAGES) {
                         stage = 0;
                         phase ^= 1u;
                     }
                 }
                 if (!ok) break;
-                mma_commit<2>(bar_tfull + 8 * acc);
+                mma_commit<CTAS>(bar_tfull + 8 * acc);  // accumulator ready for the epilogue
                 if (++acc == 2) {
                     acc = 0;
                     acc_phase ^= 1u;
                 }
             }
             if (!ok) {
-                mma_commit<2>(bar_drain);
+                // Let MMAs already issued finish before tensor memory is released.
+                mma_commit<CTAS>(bar_drain);
                 volatile uint32_t never = 0;
                 mbar_wait(bar_drain, 0, &never, kErrMmaDrain);
             }
         }
     } else {
-        // ---------------- epilogue (both CTAs): own 128 rows x BN ----------------
-        const uint32_t quad = warp % 4;
+        // ------- epilogue: 4 warps, this CTA's 128 rows x BN: TMEM -> regs -> smem -> TMA store -------
+        const uint32_t quad = warp % 4;  // tensor-memory lanes [32*quad, 32*quad + 32)
         const uint32_t epi_idx = warp - 2;
+        const uint32_t epi_tid = epi_idx * 32 + lane;
         const float sa = p.scale_a ? *p.scale_a : 1.0f;
         const float sb = p.scale_b ? *p.scale_b : 1.0f;
         const float s = sa * sb;
-        const uint32_t stage_base = base + Cfg::OFF_EPI + epi_idx * 2 * Cfg::EPI_BUF_BYTES;
-        const uint32_t peer_tfull0 = mapa_shared(bar_tfull, peer);
-        const uint32_t leader_tempty0 = mapa_shared(bar_tempty, 0);
+        const uint32_t stage_base = base + S::OFF_EPI + epi_idx * 2 * S::EPI_BUF_BYTES;
+        const uint32_t peer_tfull0 = kPair ? mapa_shared(bar_tfull, peer) : 0u;
+        const uint32_t leader_tempty0 = kPair ? mapa_shared(bar_tempty, 0) : 0u;
         int acc = 0;
         uint32_t acc_phase = 0;
         uint32_t chunk_ctr = 0;
-        for (int tile = pair_id; tile < num_tiles; tile += num_pairs) {
-            int mb, nb;
-            tile_coords(tile, p, mb, nb);
-            const bool ready = mbar_wait<true>(bar_tfull + 8 * acc, acc_phase, abort_flag, kErrEpiTmemFull);
-            if (!__all_sync(0xffffffffu, ready)) break;
-            if (leader && epi_idx == 0 && lane == 0) mbar_arrive_cluster(peer_tfull0 + 8 * acc);
-            tc_fence_after();
-            const int row0 = mb * Cfg::BM + static_cast<int>(rank) * 128 + static_cast<int>(quad) * 32;
-#pragma unroll 1
-            for (int c = 0; c < BN / Cfg::EPI_COLS; ++c) {
-                uint32_t v[64];
-                const uint32_t taddr = tmem_base + ((quad * 32u) << 16) + static_cast<uint32_t>(acc * BN + c * 64);
-                tmem_ld_32x32b_x32(taddr, *reinterpret_cast<uint32_t(*)[32]>(&v[0]));
-                tmem_ld_32x32b_x32(taddr + 32, *reinterpret_cast<uint32_t(*)[32]>(&v[32]));
-                tmem_ld_wait();
-                uint32_t packed[32];
+
+        // Scale 64 fp32 accumulators of this thread's row, round to bf16 (RNE), stage them
+        // in this warp's double-buffered 32 x 64 tile and TMA-store it at (row0, col0).
+        auto store_chunk = [&](const float (&v)[64], int row0, int col0) {
+            uint32_t packed[32];
 #pragma unroll
-                for (int j = 0; j < 32; ++j) {
-                    packed[j] = pack_bf16x2_rn(__fmul_rn(__uint_as_float(v[2 * j]), s),
-                                               __fmul_rn(__uint_as_float(v[2 * j + 1]), s));
-                }
-                const uint32_t buf = chunk_ctr & 1u;
-                if (lane == 0) bulk_wait_group_read<1>();
-                __syncwarp();
-                const uint32_t row_addr = stage_base + buf * Cfg::EPI_BUF_BYTES + lane * 128u;
-#pragma unroll
-                for (int q = 0; q < 8; ++q) {
-                    const uint32_t slot = static_cast<uint32_t>(q) ^ (lane & 7u);
-                    st_shared_v4(row_addr + slot * 16u, packed[4 * q], packed[4 * q + 1], packed[4 * q + 2],
-                                 packed[4 * q + 3]);
-                }
-                fence_proxy_async_smem();
-                __syncwarp();
-                if (lane == 0) {
-                    const int col0 = nb * BN + c * Cfg::EPI_COLS;
-                    if (row0 < p.M && col0 < p.N) {
-                        tma_store_2d(&tm_c, col0, row0, stage_base + buf * Cfg::EPI_BUF_BYTES);
-                    }
-                    bulk_commit_group();
-                }
-                ++chunk_ctr;
+            for (int j = 0; j < 32; ++j) {
+                packed[j] = pack_bf16x2_rn(__fmul_rn(v[2 * j], s), __fmul_rn(v[2 * j + 1], s));
             }
-            // All lanes' tensor-memory reads are complete (wait::ld); release the buffer.
+            const uint32_t buf = chunk_ctr & 1u;
+            // The store issued two chunks ago read this buffer; wait until it has.
+            if (lane == 0) bulk_wait_group_read<1>();
+            __syncwarp();
+            const uint32_t row_addr = stage_base + buf * S::EPI_BUF_BYTES + lane * 128u;
+#pragma unroll
+            for (int q = 0; q < 8; ++q) {
+                const uint32_t slot16 = static_cast<uint32_t>(q) ^ (lane & 7u);  // 128-byte swizzle
+                st_shared_v4(row_addr + slot16 * 16u, packed[4 * q], packed[4 * q + 1], packed[4 * q + 2],
+                             packed[4 * q + 3]);
+            }
+            fence_proxy_async_smem();
+            __syncwarp();
+            if (lane == 0) {
+                if (row0 < p.M && col0 < p.N) tma_store_2d(&tm_c, col0, row0, stage_base + buf * S::EPI_BUF_BYTES);
+                bulk_commit_group();  // an empty group when the store was skipped keeps the count exact
+            }
+            ++chunk_ctr;
+        };
+
+        auto release_accumulator = [&]() {
+            // All lanes' tensor-memory reads are complete (tcgen05.wait::ld).
             tc_fence_before();
             __syncwarp();
             if (lane == 0) {
@@ -539,16 +434,123 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(192, 1)
                 acc = 0;
                 acc_phase ^= 1u;
             }
+        };
+
+        Work w;
+        for (int idx = 0; get_work(p, slot, nslots, idx, w); ++idx) {
+            int mb, nb;
+            tile_coords(w.tile, p, mb, nb);
+            // One decision for all four epilogue warps (the stream-K path below has
+            // barriers among them, and tcgen05.ld is .sync.aligned).
+            bool ready = mbar_wait<kPair>(bar_tfull + 8 * acc, acc_phase, abort_flag, kErrEpiTmemFull);
+            ready = __all_sync(0xffffffffu, ready);
+            ready = named_bar_all(1, 128, ready);
+            __syncwarp();
+            if (!ready) break;
+            if (kPair && leader && epi_idx == 0 && lane == 0) mbar_arrive_cluster(peer_tfull0 + 8 * acc);
+            tc_fence_after();
+            const int row0 = mb * S::BM + static_cast<int>(rank) * 128 + static_cast<int>(quad) * 32;
+            const uint32_t tmem_row = tmem_base + ((quad * 32u) << 16) + static_cast<uint32_t>(acc * BN);
+
+            if (w.piece < 0) {
+#pragma unroll 1
+                for (int c = 0; c < BN / 64; ++c) {
+                    uint32_t r[64];
+                    tmem_ld_32x32b_x32(tmem_row + c * 64, *reinterpret_cast<uint32_t(*)[32]>(&r[0]));
+                    tmem_ld_32x32b_x32(tmem_row + c * 64 + 32, *reinterpret_cast<uint32_t(*)[32]>(&r[32]));
+                    tmem_ld_wait();
+                    store_chunk(*reinterpret_cast<const float(*)[64]>(&r[0]), row0, nb * BN + c * 64);
+                }
+                release_accumulator();
+                continue;
+            }
+
+            // ---- a partial piece of a stream-K tile ----
+            float* const part_base = p.partials;
+            const size_t my_part = (static_cast<size_t>(slot * 2 + w.piece) * CTAS + rank) * S::PARTIAL_FLOATS;
+#pragma unroll 1
+            for (int c = 0; c < BN / 32; ++c) {
+                uint32_t r[32];
+                tmem_ld_32x32b_x32(tmem_row + c * 32, r);
+                tmem_ld_wait();
+#pragma unroll
+                for (int j = 0; j < 32; j += 4) {
+                    float* dst = part_base + my_part + partial_offset<BN>(quad, c, j / 4, lane);
+                    st_global_v4(dst, __uint_as_float(r[j]), __uint_as_float(r[j + 1]), __uint_as_float(r[j + 2]),
+                                 __uint_as_float(r[j + 3]));
+                }
+            }
+            __threadfence();  // this thread's partial is visible GPU-wide before the count
+            named_bar_sync(1, 128);
+            const int ts = w.tile - p.dp_tiles;
+            const long long t_u0 = static_cast<long long>(ts) * p.num_k_blocks;
+            const int s_lo = sk_slot_of_unit(p, t_u0);
+            const int s_hi = sk_slot_of_unit(p, t_u0 + p.num_k_blocks - 1);
+            int* const counter = p.counters + ts * CTAS + rank;
+            if (epi_tid == 0) *bcast = atomicAdd(counter, 1);
+            named_bar_sync(1, 128);
+            const int arrived_before = *bcast;
+            if (arrived_before != s_hi - s_lo) {  // another contributor finishes this tile
+                release_accumulator();
+                continue;
+            }
+
+            // Last contributor: sum every partial in K order (deterministic whoever is
+            // last), its own straight from tensor memory, then scale and store.
+            __threadfence();
+#pragma unroll 1
+            for (int c = 0; c < BN / 64; ++c) {
+                float v[64];
+#pragma unroll
+                for (int j = 0; j < 64; ++j) v[j] = 0.0f;
+#pragma unroll 1
+                for (int sl = s_lo; sl <= s_hi; ++sl) {
+                    if (sl == slot) {
+                        uint32_t r[64];
+                        tmem_ld_32x32b_x32(tmem_row + c * 64, *reinterpret_cast<uint32_t(*)[32]>(&r[0]));
+                        tmem_ld_32x32b_x32(tmem_row + c * 64 + 32, *reinterpret_cast<uint32_t(*)[32]>(&r[32]));
+                        tmem_ld_wait();
+#pragma unroll
+                        for (int j = 0; j < 64; ++j) v[j] += __uint_as_float(r[j]);
+                        continue;
+                    }
+                    const int piece = (sk_begin(p, sl) / p.num_k_blocks == ts) ? 0 : 1;
+                    const size_t part = (static_cast<size_t>(sl * 2 + piece) * CTAS + rank) * S::PARTIAL_FLOATS;
+                    float4 x[16];
+#pragma unroll
+                    for (int h = 0; h < 2; ++h) {
+#pragma unroll
+                        for (int j = 0; j < 8; ++j) {
+                            x[8 * h + j] = __ldcg(reinterpret_cast<const float4*>(
+                                part_base + part + partial_offset<BN>(quad, 2 * c + h, j, lane)));
+                        }
+                    }
+#pragma unroll
+                    for (int j = 0; j < 16; ++j) {
+                        v[4 * j + 0] += x[j].x;
+                        v[4 * j + 1] += x[j].y;
+                        v[4 * j + 2] += x[j].z;
+                        v[4 * j + 3] += x[j].w;
+                    }
+                }
+                store_chunk(v, row0, nb * BN + c * 64);
+            }
+            release_accumulator();
+            if (epi_tid == 0) *counter = 0;  // leave the workspace ready for the next call
         }
         if (lane == 0) bulk_wait_group<0>();
         __syncwarp();
     }
 
     tc_fence_before();
-    cluster_sync();  // no CTA leaves while its peer may still signal its barriers
+    if constexpr (kPair) {
+        cluster_sync();  // no CTA leaves while its peer may still signal its barriers
+    } else {
+        __syncthreads();
+    }
     if (warp == 1) {
         tc_fence_after();
-        tmem_dealloc<2>(tmem_base, Cfg::TMEM_COLS);
+        tmem_dealloc<CTAS>(tmem_base, S::TMEM_COLS);
     }
 }
 

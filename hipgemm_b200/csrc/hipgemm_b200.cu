@@ -13,7 +13,7 @@
 #include <random>
 #include <vector>
 
-#include "../../include/hipgemm_b200.h"
+#include "hipgemm_b200.h"
 #include "gemm_sm100.cuh"
 
 namespace hg {
@@ -35,6 +35,7 @@ struct DeviceState {
     // CTA pairs this comes from cudaOccupancyMaxActiveClusters, which can be below
     // num_sms / 2 (clusters must fit inside one GPC).
     int resident_ctas[kMaxConfigs] = {};
+    cudaMemPool_t pool = nullptr;  // stream-K workspaces
 };
 
 DeviceState g_devices[kMaxDevices];
@@ -45,54 +46,56 @@ EncodeTiledFn g_encode = nullptr;
 
 struct KernelConfig {
     const char* name;
-    int bm;          // output tile rows (256 for a CTA pair)
+    int ctas;        // CTAs per tile (2 = cta_group::2 pair, launched as a 2-CTA cluster)
+    int bm;          // output tile rows (128 * ctas)
     int bn;          // output tile columns
-    int ctas;        // CTAs per tile (2 = cta_group::2 pair)
-    int b_box_rows;  // rows of B one CTA loads per K block
-    double eff;      // relative per-SM efficiency used by the automatic choice
+    int b_box_rows;  // rows of B one CTA loads per K block (bn / ctas)
+    double eff;      // relative per-SM throughput at large sizes (measured), for the choice
     int smem_bytes;
+    int partial_floats;  // one CTA's fp32 partial tile (stream-K workspace unit)
     const void* kernel;  // __global__ function pointer
     int (*launch)(const CUtensorMap&, const CUtensorMap&, const CUtensorMap&, const GemmParams&, int grid,
                   cudaStream_t);
 };
 
-template <int BN, int STAGES>
-int launch_1cta(const CUtensorMap& ta, const CUtensorMap& tb, const CUtensorMap& tc, const GemmParams& p, int grid,
-                cudaStream_t stream) {
-    using Cfg = GemmConfig<BN, STAGES>;
-    fp8_gemm_tn_sm100<BN, STAGES><<<grid, Cfg::kNumThreads, Cfg::SMEM_BYTES, stream>>>(ta, tb, tc, p);
-    return cudaGetLastError() == cudaSuccess ? HGEMM_OK : HGEMM_ERR_CUDA;
+template <int CTAS, int BN, int STAGES>
+int launch_kernel(const CUtensorMap& ta, const CUtensorMap& tb, const CUtensorMap& tc, const GemmParams& p, int grid,
+                  cudaStream_t stream) {
+    using S = KernelShape<CTAS, BN, STAGES>;
+    cudaLaunchConfig_t cfg{};
+    cfg.gridDim = dim3(static_cast<unsigned>(grid), 1, 1);
+    cfg.blockDim = dim3(S::kNumThreads, 1, 1);
+    cfg.dynamicSmemBytes = static_cast<size_t>(S::SMEM_BYTES);
+    cfg.stream = stream;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeClusterDimension;
+    attr[0].val.clusterDim.x = CTAS;
+    attr[0].val.clusterDim.y = 1;
+    attr[0].val.clusterDim.z = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = CTAS == 2 ? 1 : 0;
+    const cudaError_t e = cudaLaunchKernelEx(&cfg, fp8_gemm_tn_sm100<CTAS, BN, STAGES>, ta, tb, tc, p);
+    return e == cudaSuccess ? HGEMM_OK : HGEMM_ERR_CUDA;
 }
 
-template <int BN, int STAGES>
-KernelConfig make_1cta(const char* name, double eff) {
-    return KernelConfig{name, 128, BN, 1, BN, eff, GemmConfig<BN, STAGES>::SMEM_BYTES,
-                        reinterpret_cast<const void*>(&fp8_gemm_tn_sm100<BN, STAGES>), &launch_1cta<BN, STAGES>};
-}
-
-template <int BN, int STAGES>
-int launch_pair(const CUtensorMap& ta, const CUtensorMap& tb, const CUtensorMap& tc, const GemmParams& p, int grid,
-                cudaStream_t stream) {
-    using Cfg = PairConfig<BN, STAGES>;
-    // The cluster shape (2, 1, 1) is compiled into the kernel; grid is a multiple of 2.
-    fp8_gemm_tn_sm100_pair<BN, STAGES><<<grid, Cfg::kNumThreads, Cfg::SMEM_BYTES, stream>>>(ta, tb, tc, p);
-    return cudaGetLastError() == cudaSuccess ? HGEMM_OK : HGEMM_ERR_CUDA;
-}
-
-template <int BN, int STAGES>
-KernelConfig make_pair(const char* name, double eff) {
-    return KernelConfig{name, 256, BN, 2, BN / 2, eff, PairConfig<BN, STAGES>::SMEM_BYTES,
-                        reinterpret_cast<const void*>(&fp8_gemm_tn_sm100_pair<BN, STAGES>),
-                        &launch_pair<BN, STAGES>};
+template <int CTAS, int BN, int STAGES>
+KernelConfig make_config(const char* name, double eff) {
+    using S = KernelShape<CTAS, BN, STAGES>;
+    return KernelConfig{name,         CTAS,
+                        S::BM,        BN,
+                        S::B_ROWS,    eff,
+                        S::SMEM_BYTES, S::PARTIAL_FLOATS,
+                        reinterpret_cast<const void*>(&fp8_gemm_tn_sm100<CTAS, BN, STAGES>),
+                        &launch_kernel<CTAS, BN, STAGES>};
 }
 
 const KernelConfig kConfigs[] = {
-    {"auto", 0, 0, 0, 0, 0.0, 0, nullptr, nullptr},
-    make_1cta<256, 4>("bn256_s4", 0.93),
-    make_1cta<128, 6>("bn128_s6", 0.80),
-    make_1cta<64, 8>("bn64_s8", 0.45),
-    make_pair<256, 6>("pair256_s6", 1.0),
-    make_pair<128, 8>("pair128_s8", 0.85),
+    {"auto", 0, 0, 0, 0, 0.0, 0, 0, nullptr, nullptr},
+    make_config<1, 256, 4>("bn256_s4", 0.93),
+    make_config<1, 128, 6>("bn128_s6", 0.70),
+    make_config<1, 64, 8>("bn64_s8", 0.35),
+    make_config<2, 256, 6>("pair256_s6", 1.0),
+    make_config<2, 128, 8>("pair128_s8", 0.62),
 };
 constexpr int kNumConfigs = sizeof(kConfigs) / sizeof(kConfigs[0]);
 
@@ -148,6 +151,18 @@ int device_setup(int dev) {
             }
             st.resident_ctas[c] = clusters * k.ctas;
         }
+        // Library-owned stream-ordered pool for stream-K workspaces; it keeps its memory
+        // (release threshold = max) so repeated calls do not map pages again.
+        cudaMemPoolProps props{};
+        props.allocType = cudaMemAllocationTypePinned;
+        props.location.type = cudaMemLocationTypeDevice;
+        props.location.id = dev;
+        if (cudaMemPoolCreate(&st.pool, &props) != cudaSuccess) {
+            st.status = HGEMM_ERR_CUDA;
+            return;
+        }
+        uint64_t threshold = UINT64_MAX;
+        cudaMemPoolSetAttribute(st.pool, cudaMemPoolAttrReleaseThreshold, &threshold);
         st.num_sms = prop.multiProcessorCount;
         st.status = HGEMM_OK;
     });
@@ -176,18 +191,84 @@ bool encode_2d(CUtensorMap* map, CUtensorMapDataType dtype, size_t elem_bytes, c
                     CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
 }
 
-// Estimated relative time of a configuration: waves of output tiles over the SMs (CTA
-// pairs count as one tile slot per two SMs) times the per-SM share of one tile,
-// divided by the configuration's measured relative efficiency at large sizes.
-int choose_config(int M, int N, const DeviceState& dev) {
+// ---- schedule -------------------------------------------------------------------------
+
+// Minimum K blocks (of 128) per stream-K slot: below this a slot's partial-tile write and
+// reduction cost more than the load balance gains.
+constexpr int kMinSkUnits = 8;
+
+struct Schedule {
+    int config;
+    long tiles;
+    int slots;   // resident slots (CTAs or CTA pairs) = persistent grid / ctas
+    int grid;    // CTAs launched
+    int dp_tiles;
+    int sk_tiles;
+    int sk_slots;
+    size_t partial_bytes;  // workspace: partial tiles
+    size_t counter_bytes;  // workspace: per-tile counters (zeroed before each launch)
+};
+
+size_t align_up(size_t x, size_t a) { return (x + a - 1) / a * a; }
+
+// Splits `tiles` output tiles of `kblocks` K blocks over `slots` persistent slots into a
+// data-parallel prefix and a stream-K suffix (sc.dp_tiles, sc.sk_tiles, sc.sk_slots).
+void split_schedule(Schedule& sc, int kblocks, int schedule) {
+    sc.dp_tiles = static_cast<int>(sc.tiles);
+    sc.sk_tiles = 0;
+    sc.sk_slots = 0;
+    // The automatic schedule is data-parallel.  Measured on B200 (1024 x 8192 x 8192,
+    // 4096^3, 128 x 8192 x 8192): even with the partial-tile traffic removed, splitting the
+    // last waves along K did not beat whole tiles except on the skinny shape, where the
+    // reduction of ~5 partials per tile costs more than the balance gains.  A partly idle
+    // last wave runs its tiles faster (less contention for power and L2), which makes
+    // wave quantisation cheaper here than SM counts suggest.
+    if (schedule == HGEMM_SCHEDULE_STREAM_K) {
+        const long full = sc.tiles / sc.slots, rem = sc.tiles % sc.slots;
+        // Stream-K over the partial last wave when it gives every slot enough K; else
+        // over the last full wave plus the partial one.
+        long sk = rem;
+        if (sk == 0 || sk * kblocks < static_cast<long>(kMinSkUnits) * sc.slots) sk = std::min<long>(sc.tiles, rem + sc.slots);
+        if (full == 0) sk = sc.tiles;
+        const long units = sk * kblocks;
+        const long sk_slots = std::max<long>(1, std::min<long>(sc.slots, units / kMinSkUnits));
+        sc.sk_tiles = static_cast<int>(sk);
+        sc.dp_tiles = static_cast<int>(sc.tiles - sk);
+        sc.sk_slots = static_cast<int>(sk_slots);
+    }
+}
+
+Schedule make_schedule(int M, int N, int K, int config, int schedule, const DeviceState& dev) {
+    const KernelConfig& k = kConfigs[config];
+    Schedule sc{};
+    sc.config = config;
+    const long mblocks = (M + k.bm - 1) / k.bm, nblocks = (N + k.bn - 1) / k.bn;
+    const int kblocks = (K + 127) / 128;
+    sc.tiles = mblocks * nblocks;
+    sc.slots = std::max(1, dev.resident_ctas[config] / k.ctas);
+    split_schedule(sc, kblocks, schedule);
+    if (sc.sk_tiles > 0) {
+        sc.partial_bytes = align_up(static_cast<size_t>(sc.sk_slots) * 2 * k.ctas * k.partial_floats * 4, 256);
+        sc.counter_bytes = align_up(static_cast<size_t>(sc.sk_tiles) * k.ctas * 4, 256);
+    }
+    sc.grid = static_cast<int>(std::min<long>(sc.tiles, sc.slots)) * k.ctas;
+    if (sc.sk_tiles > 0) sc.grid = sc.slots * k.ctas;
+    return sc;
+}
+
+// Estimated relative time of a configuration under the data-parallel schedule: waves of
+// tiles over the resident slots times the per-SM share of one tile ((bm / ctas) x bn per
+// K block), divided by the configuration's measured relative efficiency.
+int choose_config(int M, int N, int K, const DeviceState& dev) {
+    (void)K;
     int best = 1;
     double best_cost = 1e300;
     for (int c = 1; c < kNumConfigs; ++c) {
         const KernelConfig& k = kConfigs[c];
-        const long tiles = static_cast<long>((M + k.bm - 1) / k.bm) * ((N + k.bn - 1) / k.bn);
-        const long slots = std::max(1, dev.resident_ctas[c] / k.ctas);
-        const long waves = (tiles + slots - 1) / slots;
-        const double cost = static_cast<double>(waves) * (k.bm / k.ctas) * k.bn / k.eff;
+        const Schedule sc = make_schedule(M, N, K, c, HGEMM_SCHEDULE_DATA_PARALLEL, dev);
+        const double area = static_cast<double>(k.bm / k.ctas) * k.bn;
+        const double work_per_slot = static_cast<double>((sc.tiles + sc.slots - 1) / sc.slots);
+        const double cost = work_per_slot * area / k.eff;
         if (cost < best_cost - 1e-9) {
             best_cost = cost;
             best = c;
@@ -198,15 +279,22 @@ int choose_config(int M, int N, const DeviceState& dev) {
 
 bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
 
-int run_gemm(const void* A, const void* B, void* C, int M, int N, int K, const float* sa, const float* sb,
-             cudaStream_t stream, int config) {
+int check_args(const void* A, const void* B, void* C, int M, int N, int K, int config, int schedule) {
     if (M < 0 || N < 0 || K < 0) return HGEMM_ERR_INVALID_VALUE;
     if (config < 0 || config >= kNumConfigs) return HGEMM_ERR_INVALID_VALUE;
+    if (schedule < HGEMM_SCHEDULE_AUTO || schedule > HGEMM_SCHEDULE_STREAM_K) return HGEMM_ERR_INVALID_VALUE;
     if (M == 0 || N == 0) return HGEMM_OK;
     if (!C || (K > 0 && (!A || !B))) return HGEMM_ERR_INVALID_VALUE;
     if (K % 16 != 0 || N % 8 != 0) return HGEMM_ERR_ALIGNMENT;
     if (!aligned16(C) || (K > 0 && (!aligned16(A) || !aligned16(B)))) return HGEMM_ERR_ALIGNMENT;
-    int rc = HGEMM_OK;
+    return HGEMM_OK;
+}
+
+// workspace == nullptr: the library allocates it from its pool, stream-ordered.
+int run_gemm(const void* A, const void* B, void* C, int M, int N, int K, const float* sa, const float* sb,
+             cudaStream_t stream, int config, int schedule, void* workspace, size_t workspace_bytes) {
+    int rc = check_args(A, B, C, M, N, K, config, schedule);
+    if (rc != HGEMM_OK || M == 0 || N == 0) return rc;
     const DeviceState* dev = current_device_setup(&rc);
     if (rc != HGEMM_OK) return rc;
     if (K == 0) {
@@ -214,8 +302,9 @@ int run_gemm(const void* A, const void* B, void* C, int M, int N, int K, const f
         return cudaMemsetAsync(C, 0, static_cast<size_t>(M) * N * 2, stream) == cudaSuccess ? HGEMM_OK
                                                                                               : HGEMM_ERR_CUDA;
     }
-    const int c = config == 0 ? choose_config(M, N, *dev) : config;
+    const int c = config == 0 ? choose_config(M, N, K, *dev) : config;
     const KernelConfig& kc = kConfigs[c];
+    const Schedule sc = make_schedule(M, N, K, c, schedule, *dev);
 
     CUtensorMap ta, tb, tc;
     if (!encode_2d(&ta, CU_TENSOR_MAP_DATA_TYPE_UINT8, 1, A, static_cast<uint64_t>(K), static_cast<uint64_t>(M), 128,
@@ -236,10 +325,25 @@ int run_gemm(const void* A, const void* B, void* C, int M, int N, int K, const f
     p.group_m = kc.ctas == 2 ? 8 : 16;
     p.scale_a = sa;
     p.scale_b = sb;
-    const long tiles = static_cast<long>(p.num_m_blocks) * p.num_n_blocks;
-    const int slots = std::max(1, dev->resident_ctas[c] / kc.ctas);
-    const int grid = static_cast<int>(std::min<long>(tiles, slots)) * kc.ctas;
-    return kc.launch(ta, tb, tc, p, grid, stream);
+    p.dp_tiles = sc.dp_tiles;
+    p.sk_tiles = sc.sk_tiles;
+    p.sk_slots = sc.sk_slots;
+    if (sc.sk_tiles == 0) return kc.launch(ta, tb, tc, p, sc.grid, stream);
+
+    const size_t need = sc.partial_bytes + sc.counter_bytes;
+    void* ws = workspace;
+    if (ws) {
+        if (workspace_bytes < need || (reinterpret_cast<uintptr_t>(ws) & 255u)) return HGEMM_ERR_INVALID_VALUE;
+    } else if (cudaMallocFromPoolAsync(&ws, need, dev->pool, stream) != cudaSuccess) {
+        cudaGetLastError();
+        return HGEMM_ERR_CUDA;
+    }
+    p.partials = static_cast<float*>(ws);
+    p.counters = reinterpret_cast<int*>(static_cast<uint8_t*>(ws) + sc.partial_bytes);
+    rc = cudaMemsetAsync(p.counters, 0, sc.counter_bytes, stream) == cudaSuccess ? HGEMM_OK : HGEMM_ERR_CUDA;
+    if (rc == HGEMM_OK) rc = kc.launch(ta, tb, tc, p, sc.grid, stream);
+    if (!workspace && cudaFreeAsync(ws, stream) != cudaSuccess && rc == HGEMM_OK) rc = HGEMM_ERR_CUDA;
+    return rc;
 }
 
 }  // namespace
@@ -249,12 +353,98 @@ extern "C" {
 
 int hgemm_fp8_tn(const void* A, const void* B, void* C, int M, int N, int K, const float* d_scale_a,
                  const float* d_scale_b, hgemm_stream_t stream) {
-    return hg::run_gemm(A, B, C, M, N, K, d_scale_a, d_scale_b, reinterpret_cast<cudaStream_t>(stream), 0);
+    return hg::run_gemm(A, B, C, M, N, K, d_scale_a, d_scale_b, reinterpret_cast<cudaStream_t>(stream), 0,
+                        HGEMM_SCHEDULE_AUTO, nullptr, 0);
 }
 
 int hgemm_fp8_tn_config(const void* A, const void* B, void* C, int M, int N, int K, const float* d_scale_a,
                         const float* d_scale_b, hgemm_stream_t stream, int config) {
-    return hg::run_gemm(A, B, C, M, N, K, d_scale_a, d_scale_b, reinterpret_cast<cudaStream_t>(stream), config);
+    return hg::run_gemm(A, B, C, M, N, K, d_scale_a, d_scale_b, reinterpret_cast<cudaStream_t>(stream), config,
+                        HGEMM_SCHEDULE_AUTO, nullptr, 0);
+}
+
+int hgemm_fp8_tn_ex(const void* A, const void* B, void* C, int M, int N, int K, const float* d_scale_a,
+                    const float* d_scale_b, hgemm_stream_t stream, int config, int schedule, void* workspace,
+                    size_t workspace_bytes) {
+    return hg::run_gemm(A, B, C, M, N, K, d_scale_a, d_scale_b, reinterpret_cast<cudaStream_t>(stream), config,
+                        schedule, workspace, workspace_bytes);
+}
+
+int hgemm_workspace_bytes(int M, int N, int K, int config, int schedule, size_t* bytes_out) {
+    const int rc0 = hg::check_args(reinterpret_cast<const void*>(16), reinterpret_cast<const void*>(16),
+                                   reinterpret_cast<void*>(16), M, N, K, config, schedule);
+    if (rc0 != HGEMM_OK) return rc0;
+    if (!bytes_out) return HGEMM_ERR_INVALID_VALUE;
+    *bytes_out = 0;
+    if (M == 0 || N == 0 || K == 0) return HGEMM_OK;
+    int rc = HGEMM_OK;
+    const hg::DeviceState* dev = hg::current_device_setup(&rc);
+    if (!dev) return rc;
+    const int c = config == 0 ? hg::choose_config(M, N, K, *dev) : config;
+    const hg::Schedule sc = hg::make_schedule(M, N, K, c, schedule, *dev);
+    *bytes_out = sc.sk_tiles > 0 ? sc.partial_bytes + sc.counter_bytes : 0;
+    return HGEMM_OK;
+}
+
+int hgemm_plan(int M, int N, int K, int config, int schedule, int* plan_out) {
+    const int rc0 = hg::check_args(reinterpret_cast<const void*>(16), reinterpret_cast<const void*>(16),
+                                   reinterpret_cast<void*>(16), M, N, K, config, schedule);
+    if (rc0 != HGEMM_OK) return rc0;
+    if (!plan_out || M <= 0 || N <= 0 || K <= 0) return HGEMM_ERR_INVALID_VALUE;
+    int rc = HGEMM_OK;
+    const hg::DeviceState* dev = hg::current_device_setup(&rc);
+    if (!dev) return rc;
+    const int c = config == 0 ? hg::choose_config(M, N, K, *dev) : config;
+    const hg::Schedule sc = hg::make_schedule(M, N, K, c, schedule, *dev);
+    plan_out[0] = c;
+    plan_out[1] = sc.grid;
+    plan_out[2] = static_cast<int>(sc.tiles);
+    plan_out[3] = sc.dp_tiles;
+    plan_out[4] = sc.sk_tiles;
+    plan_out[5] = sc.sk_slots;
+    return HGEMM_OK;
+}
+
+int hgemm_debug_schedule(long long tiles, int slots, int kblocks, int schedule, int* out3) {
+    if (tiles <= 0 || slots <= 0 || kblocks <= 0 || !out3) return HGEMM_ERR_INVALID_VALUE;
+    hg::Schedule sc{};
+    sc.tiles = tiles;
+    sc.slots = slots;
+    hg::split_schedule(sc, kblocks, schedule);
+    out3[0] = sc.dp_tiles;
+    out3[1] = sc.sk_tiles;
+    out3[2] = sc.sk_slots;
+    return HGEMM_OK;
+}
+
+int hgemm_debug_work_items(int kblocks, int nslots, int dp_tiles, int sk_tiles, int sk_slots, int slot, int* out,
+                           int max_items) {
+    if (kblocks <= 0 || nslots <= 0 || slot < 0 || slot >= nslots || !out || sk_slots < 0 ||
+        (sk_tiles > 0 && sk_slots <= 0)) {
+        return HGEMM_ERR_INVALID_VALUE;
+    }
+    hg::GemmParams p{};
+    p.num_k_blocks = kblocks;
+    p.dp_tiles = dp_tiles;
+    p.sk_tiles = sk_tiles;
+    p.sk_slots = sk_slots;
+    int n = 0;
+    hg::Work w;
+    for (int idx = 0; n < max_items && hg::get_work(p, slot, nslots, idx, w); ++idx, ++n) {
+        int* o = out + 6 * n;
+        o[0] = w.tile;
+        o[1] = w.kb_begin;
+        o[2] = w.kb_end;
+        o[3] = w.piece;
+        o[4] = 0;
+        o[5] = 0;
+        if (w.piece >= 0) {
+            const long long u0 = static_cast<long long>(w.tile - dp_tiles) * kblocks;
+            o[4] = hg::sk_slot_of_unit(p, u0);                // first contributor
+            o[5] = hg::sk_slot_of_unit(p, u0 + kblocks - 1);  // last contributor
+        }
+    }
+    return n;
 }
 
 int hgemm_fp8_tn_rows(const void* A, const void* B, void* C, int M, int N, int K, int row_begin, int row_end,
@@ -267,7 +457,7 @@ int hgemm_fp8_tn_rows(const void* A, const void* B, void* C, int M, int N, int K
     const uint8_t* a = static_cast<const uint8_t*>(A) + static_cast<size_t>(row_begin) * K;
     uint8_t* c = static_cast<uint8_t*>(C) + static_cast<size_t>(row_begin) * N * 2;
     return hg::run_gemm(a, B, c, row_end - row_begin, N, K, d_scale_a, d_scale_b,
-                        reinterpret_cast<cudaStream_t>(stream), 0);
+                        reinterpret_cast<cudaStream_t>(stream), 0, HGEMM_SCHEDULE_AUTO, nullptr, 0);
 }
 
 int hgemm_num_configs(void) { return hg::kNumConfigs; }

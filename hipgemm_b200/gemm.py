@@ -45,8 +45,13 @@ def _check_scale(name: str, s: torch.Tensor | None, device: torch.device) -> Non
 
 def fp8_gemm_tn(a: torch.Tensor, b: torch.Tensor, scale_a: torch.Tensor | None = None,
                 scale_b: torch.Tensor | None = None, out: torch.Tensor | None = None, *, config: int = 0,
+                schedule: int = 0, workspace: torch.Tensor | None = None,
                 stream: torch.cuda.Stream | None = None) -> torch.Tensor:
-    """C[M,N] (bf16) = scale_a * scale_b * a[M,K] @ b[N,K]^T, fp32 accumulation."""
+    """C[M,N] (bf16) = scale_a * scale_b * a[M,K] @ b[N,K]^T, fp32 accumulation.
+
+    config: tile configuration (0 = automatic, see config_names()); schedule: 0 automatic,
+    1 data-parallel only, 2 stream-K; workspace: optional caller-owned device buffer for a
+    stream-K schedule (else the library's stream-ordered pool is used)."""
     _check_operand("a", a)
     _check_operand("b", b)
     M, K = a.shape
@@ -61,11 +66,28 @@ def fp8_gemm_tn(a: torch.Tensor, b: torch.Tensor, scale_a: torch.Tensor | None =
         out = torch.empty((M, N), dtype=torch.bfloat16, device=a.device)
     elif out.dtype != torch.bfloat16 or tuple(out.shape) != (M, N) or not out.is_contiguous():
         raise ValueError("out must be a contiguous (M, N) bfloat16 tensor")
+    ws_ptr, ws_bytes = None, 0
+    if workspace is not None:
+        if not workspace.is_cuda or workspace.device != a.device or not workspace.is_contiguous():
+            raise ValueError("workspace must be a contiguous tensor on the operands' device")
+        ws_ptr, ws_bytes = workspace.data_ptr(), workspace.numel() * workspace.element_size()
     with torch.cuda.device(a.device):
-        rc = lib().hgemm_fp8_tn_config(_ptr(a), _ptr(b), _ptr(out), M, N, K, _ptr(scale_a), _ptr(scale_b),
-                                       _stream_handle(stream), int(config))
+        rc = lib().hgemm_fp8_tn_ex(_ptr(a), _ptr(b), _ptr(out), M, N, K, _ptr(scale_a), _ptr(scale_b),
+                                   _stream_handle(stream), int(config), int(schedule), ws_ptr, ws_bytes)
     check(rc, "hgemm_fp8_tn")
     return out
+
+
+def plan(M: int, N: int, K: int, config: int = 0, schedule: int = 0, device=None) -> dict:
+    """The launch plan the library would use on `device` (default: current)."""
+    out = (ctypes.c_int * 6)()
+    with torch.cuda.device(device if device is not None else torch.cuda.current_device()):
+        check(lib().hgemm_plan(M, N, K, config, schedule, out), "hgemm_plan")
+        nbytes = ctypes.c_size_t(0)
+        check(lib().hgemm_workspace_bytes(M, N, K, config, schedule, ctypes.byref(nbytes)), "hgemm_workspace_bytes")
+    from ._lib import config_names
+    return {"config": config_names()[out[0]], "grid": out[1], "tiles": out[2], "dp_tiles": out[3],
+            "sk_tiles": out[4], "sk_slots": out[5], "workspace_bytes": int(nbytes.value)}
 
 
 def fp8_gemm_tn_rows(a: torch.Tensor, b: torch.Tensor, out: torch.Tensor, row_begin: int, row_end: int,

@@ -65,6 +65,41 @@ int hgemm_fp8_tn_rows(const void* A, const void* B, void* C, int M, int N, int K
 int hgemm_fp8_tn_config(const void* A, const void* B, void* C, int M, int N, int K, const float* d_scale_a,
                         const float* d_scale_b, hgemm_stream_t stream, int config);
 
+/* Schedules for hgemm_fp8_tn_ex. */
+#define HGEMM_SCHEDULE_AUTO 0           /* the library's choice (currently data-parallel) */
+#define HGEMM_SCHEDULE_DATA_PARALLEL 1  /* whole output tiles only; needs no workspace */
+#define HGEMM_SCHEDULE_STREAM_K 2       /* split the last one-to-two waves of tiles along K across all
+                                           SMs; partial tiles are reduced deterministically */
+
+/* Full-control form: tile configuration (0 = automatic), schedule, and an optional
+ * caller-owned device workspace (256-byte aligned, at least hgemm_workspace_bytes(); its
+ * content on entry does not matter).  With workspace == NULL a stream-K schedule takes
+ * its workspace from a library-owned stream-ordered pool (cudaMallocFromPoolAsync /
+ * cudaFreeAsync on `stream`).  Calls that share a caller workspace must not overlap on
+ * the GPU.  No counterpart in the reference, whose launch shape is fixed. */
+int hgemm_fp8_tn_ex(const void* A, const void* B, void* C, int M, int N, int K, const float* d_scale_a,
+                    const float* d_scale_b, hgemm_stream_t stream, int config, int schedule, void* workspace,
+                    size_t workspace_bytes);
+
+/* Synchronous (device set-up).  Workspace bytes hgemm_fp8_tn_ex needs for this problem
+ * on the current device (0 when the schedule is data-parallel). */
+int hgemm_workspace_bytes(int M, int N, int K, int config, int schedule, size_t* bytes_out);
+
+/* Synchronous (device set-up).  The launch plan for this problem on the current device:
+ * plan_out[0..5] = {config, grid CTAs, output tiles, data-parallel tiles, stream-K tiles,
+ * stream-K slots}. */
+int hgemm_plan(int M, int N, int K, int config, int schedule, int* plan_out);
+
+/* Host-only views of the schedule arithmetic the kernels run (for tests):
+ * hgemm_debug_schedule splits `tiles` tiles of `kblocks` K blocks over `slots` slots and
+ * writes {data-parallel tiles, stream-K tiles, stream-K slots};
+ * hgemm_debug_work_items lists slot `slot`'s work items, 6 ints each: {tile, first K
+ * block, end K block, piece (-1 whole tile, 0/1 partial), first and last contributing
+ * slot of a partial tile}; returns the count (or a negative status). */
+int hgemm_debug_schedule(long long tiles, int slots, int kblocks, int schedule, int* out3);
+int hgemm_debug_work_items(int kblocks, int nslots, int dp_tiles, int sk_tiles, int sk_slots, int slot, int* out,
+                           int max_items);
+
 /* Number of tile configurations and their names ("bn256_s4" ...); NULL past the end. */
 int hgemm_num_configs(void);
 const char* hgemm_config_name(int config);

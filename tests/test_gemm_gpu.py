@@ -149,3 +149,54 @@ def test_against_cublaslt_scaled_mm(cuda_device):
     ref = oracle.gemm(A, B, sa, sb)
     assert oracle.validate(c_bits(ours), ref)[0] == 0
     assert oracle.validate(c_bits(lt), ref)[0] == 0
+
+
+@pytest.mark.parametrize("config", [1, 2, 3, 4, 5])
+@pytest.mark.parametrize("M,N,K", [(1000, 1032, 2064), (391, 648, 784), (128, 2048, 4096), (4000, 1024, 1152)])
+def test_stream_k_schedule(cuda_device, config, M, N, K):
+    """Forced stream-K: partial tiles reduced by their last contributor match the oracle."""
+    import hipgemm_b200 as hg
+    A, B, sa, sb = make_inputs(M, N, K, seed_a=K, seed_b=M)
+    a, b, ta, tb = to_device(A, B, sa, sb)
+    c = hg.fp8_gemm_tn(a, b, ta, tb, config=config, schedule=hg.HGEMM_SCHEDULE_STREAM_K)
+    torch.cuda.synchronize()
+    assert hg.device_status() == 0
+    bad, n, first = check_against_oracle(c_bits(c), A, B, sa, sb)
+    assert bad == 0, f"{bad}/{n} mismatches (first {first})"
+
+
+def test_stream_k_deterministic_and_workspace(cuda_device):
+    """Same bits on repeated calls (partials are summed in K order whoever finishes last),
+    with the library pool or a caller workspace; a too-small workspace is refused."""
+    import ctypes
+    import hipgemm_b200 as hg
+    M, N, K = 1024, 8192, 8192
+    A, B, sa, sb = make_inputs(M, N, K)
+    a, b, ta, tb = to_device(A, B, sa, sb)
+    pl = hg.plan(M, N, K, schedule=hg.HGEMM_SCHEDULE_STREAM_K)
+    assert pl["sk_tiles"] > 0 and pl["workspace_bytes"] > 0
+    ws = torch.empty(pl["workspace_bytes"], dtype=torch.uint8, device="cuda")
+    ws.fill_(0xAB)  # contents on entry do not matter
+    r = [hg.fp8_gemm_tn(a, b, ta, tb, schedule=hg.HGEMM_SCHEDULE_STREAM_K) for _ in range(3)]
+    r.append(hg.fp8_gemm_tn(a, b, ta, tb, schedule=hg.HGEMM_SCHEDULE_STREAM_K, workspace=ws))
+    r.append(hg.fp8_gemm_tn(a, b, ta, tb, schedule=hg.HGEMM_SCHEDULE_STREAM_K, workspace=ws))
+    torch.cuda.synchronize()
+    for x in r[1:]:
+        assert torch.equal(x.view(torch.int16), r[0].view(torch.int16))
+    rows = sample_rows(M, 64)
+    assert check_against_oracle(c_bits(r[0]), A, B, sa, sb, rows)[0] == 0
+    small = torch.empty(pl["workspace_bytes"] - 256, dtype=torch.uint8, device="cuda")
+    with pytest.raises(hg.HgemmError) as e:
+        hg.fp8_gemm_tn(a, b, ta, tb, schedule=hg.HGEMM_SCHEDULE_STREAM_K, workspace=small)
+    assert e.value.code == hg.HGEMM_ERR_INVALID_VALUE
+    assert hg.device_status() == 0
+
+
+def test_auto_plans(cuda_device):
+    import hipgemm_b200 as hg
+    assert hg.plan(8192, 8192, 8192)["config"] == "pair256_s6"
+    assert hg.plan(8192, 8192, 8192)["sk_tiles"] == 0
+    assert hg.plan(128, 8192, 8192)["sk_tiles"] == 0  # automatic schedule: data-parallel
+    assert hg.plan(128, 8192, 8192, schedule=hg.HGEMM_SCHEDULE_STREAM_K)["sk_tiles"] > 0
+    assert hg.plan(1024, 8192, 8192, schedule=hg.HGEMM_SCHEDULE_STREAM_K)["sk_tiles"] > 0
+    assert hg.plan(8192, 8192, 8192, schedule=hg.HGEMM_SCHEDULE_DATA_PARALLEL)["workspace_bytes"] == 0

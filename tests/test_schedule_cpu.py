@@ -1,0 +1,84 @@
+"""The persistent kernels' schedule arithmetic, run on the host (the same __host__
+__device__ functions the kernels call): every (tile, K block) unit of the problem is
+computed by exactly one slot, stream-K partial pieces name consistent contributor ranges,
+and each partial tile's contributors are exactly the slots that hold a piece of it."""
+import ctypes
+import itertools
+
+import pytest
+
+import hipgemm_b200 as hg
+
+
+def schedule(tiles, slots, kblocks, mode):
+    out = (ctypes.c_int * 3)()
+    assert hg.lib().hgemm_debug_schedule(tiles, slots, kblocks, mode, out) == 0
+    return tuple(out)
+
+
+def items(kblocks, nslots, dp, sk, sk_slots, slot):
+    buf = (ctypes.c_int * (6 * 4096))()
+    n = hg.lib().hgemm_debug_work_items(kblocks, nslots, dp, sk, sk_slots, slot, buf, 4096)
+    assert n >= 0
+    return [tuple(buf[6 * i:6 * i + 6]) for i in range(n)]
+
+
+CASES = [  # (tiles, slots, kblocks)
+    (1024, 74, 64), (128, 74, 64), (32, 148, 64), (112, 74, 16), (320, 74, 56), (256, 74, 32), (7168, 74, 64),
+    (1, 148, 1), (3, 148, 2), (5, 7, 3), (148, 148, 64), (149, 148, 64), (2048, 148, 64), (64, 148, 64),
+]
+
+
+@pytest.mark.parametrize("tiles,slots,kblocks", CASES)
+@pytest.mark.parametrize("mode", [hg.HGEMM_SCHEDULE_AUTO, hg.HGEMM_SCHEDULE_DATA_PARALLEL, hg.HGEMM_SCHEDULE_STREAM_K])
+def test_every_unit_exactly_once(tiles, slots, kblocks, mode):
+    dp, sk, sk_slots = schedule(tiles, slots, kblocks, mode)
+    assert dp + sk == tiles and 0 <= sk_slots <= slots
+    if mode == hg.HGEMM_SCHEDULE_DATA_PARALLEL:
+        assert sk == 0
+    if sk:
+        assert sk * kblocks >= sk_slots >= 1  # no slot gets an empty stream-K range
+    covered = {}
+    pieces = {}  # tile -> list of (slot, piece)
+    for s in range(slots):
+        for (t, k0, k1, piece, c_lo, c_hi) in items(kblocks, slots, dp, sk, sk_slots, s):
+            assert 0 <= t < tiles and 0 <= k0 < k1 <= kblocks
+            for k in range(k0, k1):
+                assert (t, k) not in covered, (t, k)
+                covered[(t, k)] = s
+            if piece < 0:
+                assert (k0, k1) == (0, kblocks)
+            else:
+                assert t >= dp and c_lo <= s <= c_hi and c_lo < c_hi
+                pieces.setdefault(t, []).append((s, piece, c_lo, c_hi))
+    assert len(covered) == tiles * kblocks
+    for t, lst in pieces.items():
+        slots_of_t = sorted(s for s, _, _, _ in lst)
+        c_lo, c_hi = lst[0][2], lst[0][3]
+        assert all((a, b) == (c_lo, c_hi) for _, _, a, b in lst)
+        assert slots_of_t == list(range(c_lo, c_hi + 1))  # contributors == slots holding a piece
+    # Each slot holds at most one piece 0 (its first stream-K tile) and one piece 1 (its
+    # last): two workspace partials per slot suffice, and piece 0 precedes piece 1.
+    for s in range(slots):
+        ps = [(t, p) for (t, _, _, p, _, _) in items(kblocks, slots, dp, sk, sk_slots, s) if p >= 0]
+        assert [p for _, p in ps] in ([], [0], [1], [0, 1])
+        if len(ps) == 2:
+            assert ps[0][0] < ps[1][0]
+
+
+def test_schedule_choices():
+    for tiles, slots in [(1024, 74), (128, 74), (32, 148), (7168, 74)]:
+        assert schedule(tiles, slots, 64, hg.HGEMM_SCHEDULE_AUTO) == (tiles, 0, 0)  # automatic = data-parallel
+    dp, sk, sks = schedule(128, 74, 64, hg.HGEMM_SCHEDULE_STREAM_K)  # 8192^3 / 8 GPUs: 1.73 waves
+    assert (dp, sk) == (74, 54) and sks == 74                       # stream-K over the partial wave
+    dp, sk, sks = schedule(32, 148, 64, hg.HGEMM_SCHEDULE_STREAM_K)  # 128 x 8192 x 8192 on 128 x 256 tiles
+    assert (dp, sk) == (0, 32) and sks == 148
+    dp, sk, sks = schedule(148, 148, 64, hg.HGEMM_SCHEDULE_STREAM_K)  # balanced: each slot gets one tile
+    assert (dp, sk, sks) == (0, 148, 148)
+
+
+def test_debug_entry_points_reject_bad_input():
+    out = (ctypes.c_int * 6)()
+    assert hg.lib().hgemm_debug_schedule(0, 74, 64, 0, out) == hg.HGEMM_ERR_INVALID_VALUE
+    assert hg.lib().hgemm_debug_work_items(64, 74, 0, 10, 0, 0, out, 1) == hg.HGEMM_ERR_INVALID_VALUE
+    assert hg.lib().hgemm_debug_work_items(64, 74, 0, 0, 0, 74, out, 1) == hg.HGEMM_ERR_INVALID_VALUE

@@ -538,3 +538,63 @@ float hgemm_host_make_quantized(uint8_t* q, size_t n, uint64_t seed, float mean,
 }
 
 }  // extern "C"
+
+// ---- allocation-free stream-K entry point -------------------------------------------------
+//
+// Some callers may not allocate device memory at all: a serving engine that has already
+// handed every byte of the GPU to its own allocator, a plugin host whose policy forbids
+// driver allocations, or a latency-critical path that cannot afford cudaMalloc's implicit
+// device-wide synchronisation.  hgemm_fp8_tn_static_scratch gives them the stream-K
+// schedule with its scratch in a fixed array that lives in this file.
+
+namespace hg {
+namespace {
+
+// 8 MiB per GPU, reserved by every GPU that loads this library until the process exits.
+constexpr size_t kStaticScratchBytes = static_cast<size_t>(8) << 20;
+static __device__ __align__(256) uint8_t g_static_scratch[kStaticScratchBytes];
+
+struct StaticScratch {
+    std::once_flag once;
+    void* ptr = nullptr;  // device address of g_static_scratch on this device
+    int status = HGEMM_ERR_CUDA;
+};
+StaticScratch g_static_scratch_ptrs[kMaxDevices];
+
+}  // namespace
+}  // namespace hg
+
+extern "C" int hgemm_fp8_tn_static_scratch(const void* A, const void* B, void* C, int M, int N, int K,
+                                           const float* d_scale_a, const float* d_scale_b, hgemm_stream_t stream) {
+    int rc = hg::check_args(A, B, C, M, N, K, 0, HGEMM_SCHEDULE_STREAM_K);
+    if (rc != HGEMM_OK || M == 0 || N == 0) return rc;
+    const hg::DeviceState* dev = hg::current_device_setup(&rc);
+    if (!dev) return rc;
+    int d = -1;
+    if (cudaGetDevice(&d) != cudaSuccess || d < 0 || d >= hg::kMaxDevices) {
+        cudaGetLastError();
+        return HGEMM_ERR_NO_DEVICE;
+    }
+    // In host code g_static_scratch names a host-side stand-in, not device memory: the
+    // device address comes from cudaGetSymbolAddress, once per device, with it current.
+    hg::StaticScratch& st = hg::g_static_scratch_ptrs[d];
+    std::call_once(st.once, [&]() {
+        void* p = nullptr;
+        if (cudaGetSymbolAddress(&p, hg::g_static_scratch) == cudaSuccess && p) {
+            st.ptr = p;
+            st.status = HGEMM_OK;
+        } else {
+            cudaGetLastError();
+        }
+    });
+    if (st.status != HGEMM_OK) return st.status;
+    if (K > 0) {
+        const int c = hg::choose_config(M, N, K, *dev);
+        const hg::Schedule sc = hg::make_schedule(M, N, K, c, HGEMM_SCHEDULE_STREAM_K, *dev);
+        if (sc.partial_bytes + sc.counter_bytes > hg::kStaticScratchBytes) return HGEMM_ERR_UNSUPPORTED;
+    }
+    // run_gemm zeroes the tile counters in the scratch (cudaMemsetAsync on `stream`) before
+    // the launch; the partial tiles are always written before they are read.
+    return hg::run_gemm(A, B, C, M, N, K, d_scale_a, d_scale_b, reinterpret_cast<cudaStream_t>(stream), 0,
+                        HGEMM_SCHEDULE_STREAM_K, st.ptr, hg::kStaticScratchBytes);
+}

@@ -90,6 +90,25 @@ int hgemm_workspace_bytes(int M, int N, int K, int config, int schedule, size_t*
  * stream-K slots}. */
 int hgemm_plan(int M, int N, int K, int config, int schedule, int* plan_out);
 
+/* Allocation-free variant of the stream-K schedule, for callers that may not allocate
+ * device memory at all (an engine that already gave all GPU memory to its own allocator,
+ * a plugin host that forbids driver allocations, a hot path that cannot take
+ * cudaMalloc's device-wide synchronisation).  No counterpart in the reference, which
+ * needs no scratch.  Same arguments and result contract as hgemm_fp8_tn; it runs the
+ * HGEMM_SCHEDULE_STREAM_K schedule with its scratch in a fixed 8 MiB device array inside
+ * this library (held by every GPU that loads the library until the process exits) and
+ * calls no cudaMalloc, cudaFree or other allocating routine.
+ * Limit: a problem whose stream-K scratch exceeds 8 MiB (see hgemm_workspace_bytes with
+ * HGEMM_SCHEDULE_STREAM_K) is refused with HGEMM_ERR_UNSUPPORTED before anything is
+ * launched; the data-parallel schedule (hgemm_fp8_tn_ex, HGEMM_SCHEDULE_DATA_PARALLEL)
+ * needs no scratch for any size.
+ * The first call on a device also looks up the array's device address; make that first
+ * call before any stream capture.  Every call shares the one array and finds the last
+ * call's contents in it (this entry point clears what must start at zero), so calls that
+ * overlap on the GPU, from any stream or thread, race: serialise them. */
+int hgemm_fp8_tn_static_scratch(const void* A, const void* B, void* C, int M, int N, int K, const float* d_scale_a,
+                                const float* d_scale_b, hgemm_stream_t stream);
+
 /* Host-only views of the schedule arithmetic the kernels run (for tests):
  * hgemm_debug_schedule splits `tiles` tiles of `kblocks` K blocks over `slots` slots and
  * writes {data-parallel tiles, stream-K tiles, stream-K slots};

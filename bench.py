@@ -342,9 +342,24 @@ def run_ours(args) -> None:
            "d2h_bytes_per_step": int(2 * hC.numel()), "steps": e2e_steps, "ms_per_step": ms_e2e}
 
     if args.allgather and world > 1:
+        from hipgemm_b200.shard import PeerCBuffers, run_allgather
         gathered = sg.gather_buffer(dev)
         ms_ag, _ = timed(lambda i: sg.all_gather(C, gathered), args.steps, 3)
-        extra["allgather"] = {"ms_per_step": ms_ag, "bytes": int(2 * M * N), "what": "NCCL all_gather of bf16 C"}
+        extra["allgather"] = {"ms_per_step": ms_ag, "bytes": int(2 * M * N), "what": "NCCL all_gather of bf16 C",
+                              "gemm_then_allgather_ms": ms + ms_ag}
+        bufs = PeerCBuffers(M, N, dev)
+
+        def fused_step(i):
+            j = i % nbuf
+            run_allgather(sg, A[j], B[j], bufs, SA[j], SB[j])
+
+        ms_f, _ = timed(fused_step, args.steps, 3)
+        extra["fused_allgather"] = {
+            "ms_per_step": ms_f, "value": flops_total / (ms_f * 1e-3) / 1e12, "unit": "TFLOP/s",
+            "what": "GEMM with every C tile TMA-stored to all ranks over NVLink (one kernel) + stream barrier"}
+        torch.cuda.synchronize()
+        barrier()
+        bufs.close()
 
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu:

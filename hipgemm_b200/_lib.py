@@ -45,6 +45,11 @@ _SIGNATURES = {
     "hgemm_plan": (_i, [_i, _i, _i, _i, _i, ctypes.POINTER(ctypes.c_int)]),
     "hgemm_debug_schedule": (_i, [ctypes.c_longlong, _i, _i, _i, ctypes.POINTER(ctypes.c_int)]),
     "hgemm_debug_work_items": (_i, [_i, _i, _i, _i, _i, _i, ctypes.POINTER(ctypes.c_int), _i]),
+    "hgemm_fp8_tn_rows_allgather": (_i, [_vp, _vp, ctypes.POINTER(ctypes.c_void_p), _i, _i, _i, _i, _i, _i, _i,
+                                        _vp, _vp, _vp]),
+    "hgemm_ipc_export": (_i, [_vp, _vp, ctypes.POINTER(ctypes.c_size_t)]),
+    "hgemm_ipc_import": (_i, [_vp, ctypes.POINTER(ctypes.c_void_p)]),
+    "hgemm_ipc_close": (_i, [_vp]),
     "hgemm_num_configs": (_i, []),
     "hgemm_config_resident_ctas": (_i, [_i]),
     "hgemm_config_name": (ctypes.c_char_p, [_i]),

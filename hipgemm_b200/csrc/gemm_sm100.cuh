@@ -63,6 +63,14 @@ struct GemmParams {
     int* counters;    // [sk tile][cta]; zero on entry, left zero on exit
 };
 
+// Extra outputs for the fused all-gather: the same C rows on other GPUs (peer memory
+// mapped into this process), written by TMA stores of the same staged tiles.
+constexpr int kMaxPeerOutputs = 7;
+struct PeerOutputs {
+    CUtensorMap maps[kMaxPeerOutputs];
+    int count;
+};
+
 // Status codes recorded by an expired bounded wait: role << 8 | site.
 enum : uint32_t {
     kErrProducerEmpty = 0x0101,
@@ -222,7 +230,8 @@ struct KernelShape {
 template <int CTAS, int BN, int STAGES>
 __global__ void __launch_bounds__(192, 1)
     fp8_gemm_tn_sm100(const __grid_constant__ CUtensorMap tm_a, const __grid_constant__ CUtensorMap tm_b,
-                      const __grid_constant__ CUtensorMap tm_c, const GemmParams p) {
+                      const __grid_constant__ CUtensorMap tm_c, const GemmParams p,
+                      const __grid_constant__ PeerOutputs peers) {
     using S = KernelShape<CTAS, BN, STAGES>;
     extern __shared__ uint8_t smem_raw[];
     // 128-byte swizzle atoms need 1024-byte alignment.
@@ -413,7 +422,12 @@ __global__ void __launch_bounds__(192, 1)
             fence_proxy_async_smem();
             __syncwarp();
             if (lane == 0) {
-                if (row0 < p.M && col0 < p.N) tma_store_2d(&tm_c, col0, row0, stage_base + buf * S::EPI_BUF_BYTES);
+                if (row0 < p.M && col0 < p.N) {
+                    const uint32_t src = stage_base + buf * S::EPI_BUF_BYTES;
+                    tma_store_2d(&tm_c, col0, row0, src);
+                    // Fused all-gather: the same tile into every peer's copy of these rows.
+                    for (int i = 0; i < peers.count; ++i) tma_store_2d(&peers.maps[i], col0, row0, src);
+                }
                 bulk_commit_group();  // an empty group when the store was skipped keeps the count exact
             }
             ++chunk_ctr;

@@ -41,6 +41,8 @@ struct DeviceState {
 DeviceState g_devices[kMaxDevices];
 std::once_flag g_encode_once;
 EncodeTiledFn g_encode = nullptr;
+using AddressRangeFn = CUresult (*)(CUdeviceptr*, size_t*, CUdeviceptr);
+AddressRangeFn g_address_range = nullptr;
 
 // ---- kernel configurations ----------------------------------------------------------
 
@@ -54,13 +56,13 @@ struct KernelConfig {
     int smem_bytes;
     int partial_floats;  // one CTA's fp32 partial tile (stream-K workspace unit)
     const void* kernel;  // __global__ function pointer
-    int (*launch)(const CUtensorMap&, const CUtensorMap&, const CUtensorMap&, const GemmParams&, int grid,
-                  cudaStream_t);
+    int (*launch)(const CUtensorMap&, const CUtensorMap&, const CUtensorMap&, const GemmParams&,
+                  const PeerOutputs&, int grid, cudaStream_t);
 };
 
 template <int CTAS, int BN, int STAGES>
-int launch_kernel(const CUtensorMap& ta, const CUtensorMap& tb, const CUtensorMap& tc, const GemmParams& p, int grid,
-                  cudaStream_t stream) {
+int launch_kernel(const CUtensorMap& ta, const CUtensorMap& tb, const CUtensorMap& tc, const GemmParams& p,
+                  const PeerOutputs& peers, int grid, cudaStream_t stream) {
     using S = KernelShape<CTAS, BN, STAGES>;
     cudaLaunchConfig_t cfg{};
     cfg.gridDim = dim3(static_cast<unsigned>(grid), 1, 1);
@@ -74,7 +76,7 @@ int launch_kernel(const CUtensorMap& ta, const CUtensorMap& tb, const CUtensorMa
     attr[0].val.clusterDim.z = 1;
     cfg.attrs = attr;
     cfg.numAttrs = CTAS == 2 ? 1 : 0;
-    const cudaError_t e = cudaLaunchKernelEx(&cfg, fp8_gemm_tn_sm100<CTAS, BN, STAGES>, ta, tb, tc, p);
+    const cudaError_t e = cudaLaunchKernelEx(&cfg, fp8_gemm_tn_sm100<CTAS, BN, STAGES>, ta, tb, tc, p, peers);
     return e == cudaSuccess ? HGEMM_OK : HGEMM_ERR_CUDA;
 }
 
@@ -105,6 +107,11 @@ void init_encode() {
     if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &fn, cudaEnableDefault, &q) == cudaSuccess &&
         q == cudaDriverEntryPointSuccess) {
         g_encode = reinterpret_cast<EncodeTiledFn>(fn);
+    }
+    fn = nullptr;
+    if (cudaGetDriverEntryPoint("cuMemGetAddressRange", &fn, cudaEnableDefault, &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess) {
+        g_address_range = reinterpret_cast<AddressRangeFn>(fn);
     }
 }
 
@@ -291,16 +298,21 @@ int check_args(const void* A, const void* B, void* C, int M, int N, int K, int c
 }
 
 // workspace == nullptr: the library allocates it from its pool, stream-ordered.
+// peer_c[0..n_peer): more M x N outputs (same layout as C) that receive every C tile too.
 int run_gemm(const void* A, const void* B, void* C, int M, int N, int K, const float* sa, const float* sb,
-             cudaStream_t stream, int config, int schedule, void* workspace, size_t workspace_bytes) {
+             cudaStream_t stream, int config, int schedule, void* workspace, size_t workspace_bytes,
+             void* const* peer_c = nullptr, int n_peer = 0) {
     int rc = check_args(A, B, C, M, N, K, config, schedule);
     if (rc != HGEMM_OK || M == 0 || N == 0) return rc;
     const DeviceState* dev = current_device_setup(&rc);
     if (rc != HGEMM_OK) return rc;
     if (K == 0) {
         // An empty sum: every element is bf16(+0), as the reference's acc = 0.0f gives.
-        return cudaMemsetAsync(C, 0, static_cast<size_t>(M) * N * 2, stream) == cudaSuccess ? HGEMM_OK
-                                                                                              : HGEMM_ERR_CUDA;
+        for (int i = -1; i < n_peer; ++i) {
+            void* dst = i < 0 ? C : peer_c[i];
+            if (cudaMemsetAsync(dst, 0, static_cast<size_t>(M) * N * 2, stream) != cudaSuccess) return HGEMM_ERR_CUDA;
+        }
+        return HGEMM_OK;
     }
     const int c = config == 0 ? choose_config(M, N, K, *dev) : config;
     const KernelConfig& kc = kConfigs[c];
@@ -315,6 +327,15 @@ int run_gemm(const void* A, const void* B, void* C, int M, int N, int K, const f
                    32)) {
         return HGEMM_ERR_CUDA;
     }
+    PeerOutputs peers{};
+    if (n_peer < 0 || n_peer > kMaxPeerOutputs) return HGEMM_ERR_INVALID_VALUE;
+    for (int i = 0; i < n_peer; ++i) {
+        if (!encode_2d(&peers.maps[i], CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, peer_c[i], static_cast<uint64_t>(N),
+                       static_cast<uint64_t>(M), 64, 32)) {
+            return HGEMM_ERR_CUDA;
+        }
+    }
+    peers.count = n_peer;
     GemmParams p{};
     p.M = M;
     p.N = N;
@@ -328,7 +349,7 @@ int run_gemm(const void* A, const void* B, void* C, int M, int N, int K, const f
     p.dp_tiles = sc.dp_tiles;
     p.sk_tiles = sc.sk_tiles;
     p.sk_slots = sc.sk_slots;
-    if (sc.sk_tiles == 0) return kc.launch(ta, tb, tc, p, sc.grid, stream);
+    if (sc.sk_tiles == 0) return kc.launch(ta, tb, tc, p, peers, sc.grid, stream);
 
     const size_t need = sc.partial_bytes + sc.counter_bytes;
     void* ws = workspace;
@@ -341,7 +362,7 @@ int run_gemm(const void* A, const void* B, void* C, int M, int N, int K, const f
     p.partials = static_cast<float*>(ws);
     p.counters = reinterpret_cast<int*>(static_cast<uint8_t*>(ws) + sc.partial_bytes);
     rc = cudaMemsetAsync(p.counters, 0, sc.counter_bytes, stream) == cudaSuccess ? HGEMM_OK : HGEMM_ERR_CUDA;
-    if (rc == HGEMM_OK) rc = kc.launch(ta, tb, tc, p, sc.grid, stream);
+    if (rc == HGEMM_OK) rc = kc.launch(ta, tb, tc, p, peers, sc.grid, stream);
     if (!workspace && cudaFreeAsync(ws, stream) != cudaSuccess && rc == HGEMM_OK) rc = HGEMM_ERR_CUDA;
     return rc;
 }
@@ -445,6 +466,71 @@ int hgemm_debug_work_items(int kblocks, int nslots, int dp_tiles, int sk_tiles, 
         }
     }
     return n;
+}
+
+int hgemm_fp8_tn_rows_allgather(const void* A, const void* B, void* const* C_ranks, int nranks, int rank, int M,
+                                int N, int K, int row_begin, int row_end, const float* d_scale_a,
+                                const float* d_scale_b, hgemm_stream_t stream) {
+    if (nranks < 1 || nranks > hg::kMaxPeerOutputs + 1 || rank < 0 || rank >= nranks || !C_ranks) {
+        return HGEMM_ERR_INVALID_VALUE;
+    }
+    if (M < 0 || N < 0 || K < 0 || row_begin < 0 || row_end < row_begin || row_end > M) {
+        return HGEMM_ERR_INVALID_VALUE;
+    }
+    for (int i = 0; i < nranks; ++i) {
+        if (!C_ranks[i]) return HGEMM_ERR_INVALID_VALUE;
+        if (reinterpret_cast<uintptr_t>(C_ranks[i]) & 15u) return HGEMM_ERR_ALIGNMENT;
+    }
+    if (row_end == row_begin || N == 0) return HGEMM_OK;
+    if (!A) return HGEMM_ERR_INVALID_VALUE;
+    const size_t row_bytes = static_cast<size_t>(N) * 2;
+    const uint8_t* a = static_cast<const uint8_t*>(A) + static_cast<size_t>(row_begin) * K;
+    void* local = static_cast<uint8_t*>(C_ranks[rank]) + static_cast<size_t>(row_begin) * row_bytes;
+    void* peers[hg::kMaxPeerOutputs];
+    int n = 0;
+    for (int i = 0; i < nranks; ++i) {
+        if (i != rank) peers[n++] = static_cast<uint8_t*>(C_ranks[i]) + static_cast<size_t>(row_begin) * row_bytes;
+    }
+    return hg::run_gemm(a, B, local, row_end - row_begin, N, K, d_scale_a, d_scale_b,
+                        reinterpret_cast<cudaStream_t>(stream), 0, HGEMM_SCHEDULE_DATA_PARALLEL, nullptr, 0, peers, n);
+}
+
+int hgemm_ipc_export(const void* ptr, void* handle_out, size_t* offset_out) {
+    if (!ptr || !handle_out || !offset_out) return HGEMM_ERR_INVALID_VALUE;
+    int rc = HGEMM_OK;
+    if (!hg::current_device_setup(&rc)) return rc;
+    if (!hg::g_address_range) return HGEMM_ERR_CUDA;
+    CUdeviceptr base = 0;
+    size_t size = 0;
+    if (hg::g_address_range(&base, &size, reinterpret_cast<CUdeviceptr>(ptr)) != CUDA_SUCCESS) return HGEMM_ERR_CUDA;
+    cudaIpcMemHandle_t h;
+    if (cudaIpcGetMemHandle(&h, reinterpret_cast<void*>(base)) != cudaSuccess) {
+        cudaGetLastError();
+        return HGEMM_ERR_CUDA;
+    }
+    std::memcpy(handle_out, &h, sizeof(h));
+    *offset_out = static_cast<size_t>(reinterpret_cast<CUdeviceptr>(ptr) - base);
+    return HGEMM_OK;
+}
+
+int hgemm_ipc_import(const void* handle, void** base_out) {
+    if (!handle || !base_out) return HGEMM_ERR_INVALID_VALUE;
+    cudaIpcMemHandle_t h;
+    std::memcpy(&h, handle, sizeof(h));
+    if (cudaIpcOpenMemHandle(base_out, h, cudaIpcMemLazyEnablePeerAccess) != cudaSuccess) {
+        cudaGetLastError();
+        return HGEMM_ERR_CUDA;
+    }
+    return HGEMM_OK;
+}
+
+int hgemm_ipc_close(void* base) {
+    if (!base) return HGEMM_ERR_INVALID_VALUE;
+    if (cudaIpcCloseMemHandle(base) != cudaSuccess) {
+        cudaGetLastError();
+        return HGEMM_ERR_CUDA;
+    }
+    return HGEMM_OK;
 }
 
 int hgemm_fp8_tn_rows(const void* A, const void* B, void* C, int M, int N, int K, int row_begin, int row_end,

@@ -9,10 +9,13 @@ there and follows the row partition the benchmark configs prescribe.
 """
 from __future__ import annotations
 
+import ctypes
+
 import torch
 import torch.distributed as dist
 
-from .gemm import fp8_gemm_tn
+from ._lib import check, lib
+from .gemm import _check_operand, _ptr, _stream_handle, fp8_gemm_tn
 
 
 def row_range(M: int, rank: int, world: int) -> tuple[int, int]:
@@ -80,3 +83,76 @@ class ShardedGemm:
             r0, r1 = row_range(self.M, r, self.world)
             parts.append(gathered[r * self.pad_rows: r * self.pad_rows + (r1 - r0)])
         return torch.cat(parts, dim=0)
+
+
+class PeerCBuffers:
+    """A full M x N bf16 C on every rank of `group`, each rank's buffer mapped into every
+    other rank's process with CUDA IPC, for ShardedGemm.run_allgather.  Collective:
+    every rank constructs it (and closes it) together."""
+
+    def __init__(self, M: int, N: int, device: torch.device, group=None):
+        self.M, self.N, self.group = M, N, group
+        self.world = dist.get_world_size(group) if dist.is_initialized() else 1
+        self.rank = dist.get_rank(group) if dist.is_initialized() else 0
+        self.local = torch.empty((M, N), dtype=torch.bfloat16, device=device)
+        self._bases: list[int] = []
+        handle = (ctypes.c_uint8 * 64)()
+        offset = ctypes.c_size_t(0)
+        with torch.cuda.device(device):
+            check(lib().hgemm_ipc_export(self.local.data_ptr(), handle, ctypes.byref(offset)), "hgemm_ipc_export")
+        mine = (bytes(handle), int(offset.value))
+        allh = [None] * self.world
+        if self.world > 1:
+            dist.all_gather_object(allh, mine, group=group)
+        else:
+            allh = [mine]
+        ptrs = []
+        for r, (h, off) in enumerate(allh):
+            if r == self.rank:
+                ptrs.append(self.local.data_ptr())
+                continue
+            base = ctypes.c_void_p(0)
+            buf = (ctypes.c_uint8 * 64).from_buffer_copy(h)
+            with torch.cuda.device(device):
+                check(lib().hgemm_ipc_import(buf, ctypes.byref(base)), "hgemm_ipc_import")
+            self._bases.append(int(base.value))
+            ptrs.append(int(base.value) + off)
+        self.ptrs = (ctypes.c_void_p * self.world)(*ptrs)
+
+    def close(self) -> None:
+        """Unmaps the peers' buffers (call on every rank, after the last use)."""
+        for b in self._bases:
+            check(lib().hgemm_ipc_close(ctypes.c_void_p(b)), "hgemm_ipc_close")
+        self._bases = []
+
+
+def stream_barrier(group=None) -> None:
+    """Orders a one-element NCCL all-reduce on the current stream: work queued after it
+    starts only once every rank's preceding work has completed."""
+    if dist.is_initialized() and dist.get_world_size(group) > 1:
+        t = torch.zeros(1, dtype=torch.float32, device=torch.cuda.current_device())
+        dist.all_reduce(t, group=group)
+
+
+def run_allgather(sg: ShardedGemm, a_rows: torch.Tensor, b: torch.Tensor, bufs: PeerCBuffers, scale_a=None,
+                  scale_b=None, barrier: bool = True) -> torch.Tensor:
+    """This rank's rows of C = A . B^T computed and written into every rank's full C in
+    one kernel (hgemm_fp8_tn_rows_allgather); with barrier=True, a stream barrier
+    follows so that bufs.local holds the whole C for work queued after this call."""
+    _check_operand("a_rows", a_rows)
+    _check_operand("b", b)
+    if tuple(a_rows.shape) != (sg.rows, sg.K) or tuple(b.shape) != (sg.N, sg.K):
+        raise ValueError("shard shapes do not match the partition")
+    if (bufs.M, bufs.N) != (sg.M, sg.N) or bufs.world != sg.world or bufs.rank != sg.rank:
+        raise ValueError("buffers do not match the partition")
+    # a_rows holds rows [row_begin, row_end): pass its pointer as the base of rows
+    # [0, rows) of a virtual full A, i.e. shift by -row_begin rows.
+    a_base = a_rows.data_ptr() - sg.row_begin * sg.K
+    with torch.cuda.device(a_rows.device):
+        rc = lib().hgemm_fp8_tn_rows_allgather(a_base, _ptr(b), bufs.ptrs, sg.world, sg.rank, sg.M, sg.N, sg.K,
+                                               sg.row_begin, sg.row_end, _ptr(scale_a), _ptr(scale_b),
+                                               _stream_handle(None))
+    check(rc, "hgemm_fp8_tn_rows_allgather")
+    if barrier:
+        stream_barrier(sg.group)
+    return bufs.local

@@ -60,6 +60,27 @@ int hgemm_fp8_tn(const void* A, const void* B, void* C, int M, int N, int K, con
 int hgemm_fp8_tn_rows(const void* A, const void* B, void* C, int M, int N, int K, int row_begin, int row_end,
                       const float* d_scale_a, const float* d_scale_b, hgemm_stream_t stream);
 
+/* The M-sharded call fused with the all-gather of C.  C_ranks[i] is rank i's full M x N
+ * C buffer as mapped into this process (C_ranks[rank] is this GPU's own; the others are
+ * peer memory opened with hgemm_ipc_import, 1 <= nranks <= 8).  Rows [row_begin, row_end)
+ * are computed here and every finished C tile is TMA-stored into all nranks buffers, so
+ * the exchange over NVLink overlaps the math tile by tile.  When every rank's call has
+ * completed (order a barrier after it on the stream, e.g. a one-element NCCL all-reduce),
+ * every buffer holds the whole C.  A caller that reuses the buffers must also put a
+ * barrier between its last read of C and the next call.  No counterpart in the
+ * reference, which is single-GPU (its C is written by one kernel, test.cpp:79). */
+int hgemm_fp8_tn_rows_allgather(const void* A, const void* B, void* const* C_ranks, int nranks, int rank, int M,
+                                int N, int K, int row_begin, int row_end, const float* d_scale_a,
+                                const float* d_scale_b, hgemm_stream_t stream);
+
+/* CUDA IPC helpers for the buffers above (synchronous).  hgemm_ipc_export writes the 64-byte
+ * handle of the allocation that contains `ptr` and ptr's offset inside it;
+ * hgemm_ipc_import opens a handle from another process (returns the allocation's base:
+ * add the offset), hgemm_ipc_close releases it. */
+int hgemm_ipc_export(const void* ptr, void* handle_out, size_t* offset_out);
+int hgemm_ipc_import(const void* handle, void** base_out);
+int hgemm_ipc_close(void* base);
+
 /* Same as hgemm_fp8_tn with the tile configuration forced (benchmarks and tests):
  * config 0 = automatic choice; see hgemm_config_name() for the others. */
 int hgemm_fp8_tn_config(const void* A, const void* B, void* C, int M, int N, int K, const float* d_scale_a,

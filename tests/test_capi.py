@@ -104,3 +104,22 @@ def test_header_template_rejects_bad_shapes(tmp_path):
     r = subprocess.run(["g++", "-std=c++17", "-fsyntax-only", "-I", os.path.dirname(HEADER), str(cpp)],
                        capture_output=True, text=True)
     assert r.returncode != 0 and "multiple of 16" in r.stderr
+
+
+def test_fused_allgather_and_ipc_argument_checks():
+    L = hg.lib()
+    ptrs = (ctypes.c_void_p * 2)(FAKE, FAKE)
+    bad = (ctypes.c_void_p * 2)(FAKE, None)
+    mis = (ctypes.c_void_p * 2)(FAKE, FAKE + 2)
+    args = (FAKE, FAKE)
+    assert L.hgemm_fp8_tn_rows_allgather(*args, ptrs, 0, 0, 8, 8, 16, 0, 8, None, None, None) == hg.HGEMM_ERR_INVALID_VALUE
+    assert L.hgemm_fp8_tn_rows_allgather(*args, ptrs, 9, 0, 8, 8, 16, 0, 8, None, None, None) == hg.HGEMM_ERR_INVALID_VALUE
+    assert L.hgemm_fp8_tn_rows_allgather(*args, ptrs, 2, 2, 8, 8, 16, 0, 8, None, None, None) == hg.HGEMM_ERR_INVALID_VALUE
+    assert L.hgemm_fp8_tn_rows_allgather(*args, None, 2, 0, 8, 8, 16, 0, 8, None, None, None) == hg.HGEMM_ERR_INVALID_VALUE
+    assert L.hgemm_fp8_tn_rows_allgather(*args, bad, 2, 0, 8, 8, 16, 0, 8, None, None, None) == hg.HGEMM_ERR_INVALID_VALUE
+    assert L.hgemm_fp8_tn_rows_allgather(*args, mis, 2, 0, 8, 8, 16, 0, 8, None, None, None) == hg.HGEMM_ERR_ALIGNMENT
+    assert L.hgemm_fp8_tn_rows_allgather(*args, ptrs, 2, 0, 8, 8, 16, 5, 9, None, None, None) == hg.HGEMM_ERR_INVALID_VALUE
+    assert L.hgemm_fp8_tn_rows_allgather(*args, ptrs, 2, 1, 8, 8, 16, 4, 4, None, None, None) == hg.HGEMM_OK
+    assert L.hgemm_ipc_export(None, None, None) == hg.HGEMM_ERR_INVALID_VALUE
+    assert L.hgemm_ipc_import(None, None) == hg.HGEMM_ERR_INVALID_VALUE
+    assert L.hgemm_ipc_close(None) == hg.HGEMM_ERR_INVALID_VALUE

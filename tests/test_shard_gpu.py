@@ -63,3 +63,53 @@ def test_sharded_gemm_matches_single_gpu(tmp_path, M, N, K):
                        start_method="spawn", join=True)
     same, ok_oracle = np.load(tmp_path / "ok.npy")
     assert same and ok_oracle
+
+
+def _fused_worker(rank, world, port, M, N, K, out_dir):
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port), NCCL_NVLS_ENABLE="0")
+    torch.cuda.set_device(rank)
+    dev = torch.device("cuda", rank)
+    dist.init_process_group("nccl", rank=rank, world_size=world, timeout=datetime.timedelta(seconds=60),
+                            device_id=dev)
+    bufs = None
+    try:
+        import oracle
+        import hipgemm_b200 as hg
+        from hipgemm_b200.shard import PeerCBuffers, ShardedGemm, run_allgather, stream_barrier
+        A, sa = oracle.make_quantized((M, K), 0)
+        B, sb = oracle.make_quantized((N, K), 1)
+        sg = ShardedGemm(M, N, K)
+        a = torch.from_numpy(np.ascontiguousarray(A[sg.row_begin:sg.row_end])).to(dev)
+        b = torch.from_numpy(B).to(dev)
+        ta = torch.tensor([sa], dtype=torch.float32, device=dev)
+        tb = torch.tensor([sb], dtype=torch.float32, device=dev)
+        bufs = PeerCBuffers(M, N, dev)
+        single = hg.fp8_gemm_tn(torch.from_numpy(A).to(dev), b, ta, tb)
+        ok = True
+        for step in range(2):  # twice: the buffers are rewritten in place
+            bufs.local.fill_(float("nan"))
+            stream_barrier()  # nobody writes into a buffer before its owner has cleared it
+            full = run_allgather(sg, a, b, bufs, ta, tb)
+            torch.cuda.synchronize()
+            ok = ok and torch.equal(full.view(torch.int16), single.view(torch.int16))
+        ok = ok and hg.device_status() == 0
+        np.save(os.path.join(out_dir, f"fused{rank}.npy"), np.array([ok]))
+        stream_barrier()
+        torch.cuda.synchronize()
+    finally:
+        if bufs is not None:
+            bufs.close()
+        dist.destroy_process_group()
+
+
+@pytest.mark.parametrize("M,N,K", [(4096, 2048, 1024), (1000, 1032, 528)])
+def test_fused_allgather_gives_every_rank_the_full_product(tmp_path, M, N, K):
+    """GEMM + all-gather in one kernel: every rank's C buffer equals the single-GPU C."""
+    n = torch.cuda.device_count()
+    if n < 2:
+        pytest.skip("needs at least two GPUs")
+    world = min(n, 8)
+    mp.start_processes(_fused_worker, args=(world, _free_port(), M, N, K, str(tmp_path)), nprocs=world,
+                       start_method="spawn", join=True)
+    for r in range(world):
+        assert bool(np.load(tmp_path / f"fused{r}.npy")[0]), f"rank {r}"

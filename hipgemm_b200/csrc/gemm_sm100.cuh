@@ -208,8 +208,10 @@ struct KernelShape {
     static constexpr int A_BYTES = 128 * BK;
     static constexpr int B_BYTES = B_ROWS * BK;
     static constexpr int STAGE_BYTES = A_BYTES + B_BYTES;
-    static constexpr int EPI_COLS = 64;                      // bf16 columns per staged chunk (128 B)
-    static constexpr int EPI_BUF_BYTES = 32 * EPI_COLS * 2;  // one warp's 32 rows x 128 B
+    // bf16 columns per staged epilogue chunk: 64 (128-byte rows, 128-byte swizzle) when
+    // BN allows, else 32 (64-byte rows, 64-byte swizzle).
+    static constexpr int EPI_COLS = BN % 64 == 0 ? 64 : 32;
+    static constexpr int EPI_BUF_BYTES = 32 * 64 * 2;  // one warp's 32 rows x 128 B (either width fits)
     static constexpr int OFF_A = 0;
     static constexpr int OFF_B = OFF_A + STAGES * A_BYTES;
     static constexpr int OFF_EPI = OFF_B + STAGES * B_BYTES;
@@ -217,11 +219,14 @@ struct KernelShape {
     static constexpr int NUM_BARS = 2 * STAGES + 5;  // full, empty, tfull x2, tempty x2, drain
     static constexpr int OFF_MISC = OFF_BAR + NUM_BARS * 8;
     static constexpr int SMEM_BYTES = OFF_MISC + 16 + 1024;  // + slack to align the base to 1024 B
-    static constexpr uint32_t TMEM_COLS = 2 * BN < 32 ? 32 : 2 * BN;
+    // Two accumulators of BN fp32 columns, rounded up to the power of two tcgen05.alloc takes.
+    static constexpr uint32_t TMEM_COLS =
+        2 * BN <= 32 ? 32 : (2 * BN <= 64 ? 64 : (2 * BN <= 128 ? 128 : (2 * BN <= 256 ? 256 : 512)));
     static constexpr uint32_t IDESC = idesc_e4m3_f32(BM, BN);
     static constexpr int PARTIAL_FLOATS = 128 * BN;  // one CTA's share of a partial tile
     static_assert(CTAS == 1 || CTAS == 2, "one CTA or a CTA pair");
-    static_assert(BN % 64 == 0 && BN >= 64 && BN <= 256, "BN must be 64, 128, 192 or 256");
+    static_assert(BN % 32 == 0 && BN >= 64 && BN <= 256, "BN must be a multiple of 32 in [64, 256]");
+    static_assert(CTAS == 1 || BN % 16 == 0, "M=256 MMAs need N % 16 == 0");
     static_assert(B_BYTES % 1024 == 0, "B tiles must keep 1024-byte alignment");
     static_assert((TMEM_COLS & (TMEM_COLS - 1)) == 0, "tensor memory allocations are powers of two");
     static_assert(SMEM_BYTES <= 232448, "exceeds 227 KB of shared memory per CTA");
@@ -400,22 +405,27 @@ __global__ void __launch_bounds__(192, 1)
         uint32_t acc_phase = 0;
         uint32_t chunk_ctr = 0;
 
-        // Scale 64 fp32 accumulators of this thread's row, round to bf16 (RNE), stage them
-        // in this warp's double-buffered 32 x 64 tile and TMA-store it at (row0, col0).
-        auto store_chunk = [&](const float (&v)[64], int row0, int col0) {
-            uint32_t packed[32];
+        constexpr int EC = S::EPI_COLS;
+
+        // Scale EC fp32 accumulators of this thread's row, round to bf16 (RNE), stage them
+        // in this warp's double-buffered 32 x EC tile and TMA-store it at (row0, col0).
+        auto store_chunk = [&](const float (&v)[EC], int row0, int col0) {
+            uint32_t packed[EC / 2];
 #pragma unroll
-            for (int j = 0; j < 32; ++j) {
+            for (int j = 0; j < EC / 2; ++j) {
                 packed[j] = pack_bf16x2_rn(__fmul_rn(v[2 * j], s), __fmul_rn(v[2 * j + 1], s));
             }
             const uint32_t buf = chunk_ctr & 1u;
             // The store issued two chunks ago read this buffer; wait until it has.
             if (lane == 0) bulk_wait_group_read<1>();
             __syncwarp();
-            const uint32_t row_addr = stage_base + buf * S::EPI_BUF_BYTES + lane * 128u;
+            const uint32_t row_addr = stage_base + buf * S::EPI_BUF_BYTES + lane * (EC * 2u);
 #pragma unroll
-            for (int q = 0; q < 8; ++q) {
-                const uint32_t slot16 = static_cast<uint32_t>(q) ^ (lane & 7u);  // 128-byte swizzle
+            for (int q = 0; q < EC / 8; ++q) {
+                // 16-byte group q of row `lane` in the TMA swizzle: 128-byte mode XORs with
+                // row % 8, 64-byte mode with (row / 2) % 4 (address bits [7:9] / [7:8]).
+                const uint32_t slot16 = EC == 64 ? (static_cast<uint32_t>(q) ^ (lane & 7u))
+                                                 : (static_cast<uint32_t>(q) ^ ((lane >> 1) & 3u));
                 st_shared_v4(row_addr + slot16 * 16u, packed[4 * q], packed[4 * q + 1], packed[4 * q + 2],
                              packed[4 * q + 3]);
             }
@@ -468,12 +478,14 @@ __global__ void __launch_bounds__(192, 1)
 
             if (w.piece < 0) {
 #pragma unroll 1
-                for (int c = 0; c < BN / 64; ++c) {
-                    uint32_t r[64];
-                    tmem_ld_32x32b_x32(tmem_row + c * 64, *reinterpret_cast<uint32_t(*)[32]>(&r[0]));
-                    tmem_ld_32x32b_x32(tmem_row + c * 64 + 32, *reinterpret_cast<uint32_t(*)[32]>(&r[32]));
+                for (int c = 0; c < BN / EC; ++c) {
+                    uint32_t r[EC];
+#pragma unroll
+                    for (int h = 0; h < EC / 32; ++h) {
+                        tmem_ld_32x32b_x32(tmem_row + c * EC + 32 * h, *reinterpret_cast<uint32_t(*)[32]>(&r[32 * h]));
+                    }
                     tmem_ld_wait();
-                    store_chunk(*reinterpret_cast<const float(*)[64]>(&r[0]), row0, nb * BN + c * 64);
+                    store_chunk(*reinterpret_cast<const float(*)[EC]>(&r[0]), row0, nb * BN + c * EC);
                 }
                 release_accumulator();
                 continue;
@@ -513,41 +525,44 @@ __global__ void __launch_bounds__(192, 1)
             // last), its own straight from tensor memory, then scale and store.
             __threadfence();
 #pragma unroll 1
-            for (int c = 0; c < BN / 64; ++c) {
-                float v[64];
+            for (int c = 0; c < BN / EC; ++c) {
+                float v[EC];
 #pragma unroll
-                for (int j = 0; j < 64; ++j) v[j] = 0.0f;
+                for (int j = 0; j < EC; ++j) v[j] = 0.0f;
 #pragma unroll 1
                 for (int sl = s_lo; sl <= s_hi; ++sl) {
                     if (sl == slot) {
-                        uint32_t r[64];
-                        tmem_ld_32x32b_x32(tmem_row + c * 64, *reinterpret_cast<uint32_t(*)[32]>(&r[0]));
-                        tmem_ld_32x32b_x32(tmem_row + c * 64 + 32, *reinterpret_cast<uint32_t(*)[32]>(&r[32]));
+                        uint32_t r[EC];
+#pragma unroll
+                        for (int h = 0; h < EC / 32; ++h) {
+                            tmem_ld_32x32b_x32(tmem_row + c * EC + 32 * h,
+                                               *reinterpret_cast<uint32_t(*)[32]>(&r[32 * h]));
+                        }
                         tmem_ld_wait();
 #pragma unroll
-                        for (int j = 0; j < 64; ++j) v[j] += __uint_as_float(r[j]);
+                        for (int j = 0; j < EC; ++j) v[j] += __uint_as_float(r[j]);
                         continue;
                     }
                     const int piece = (sk_begin(p, sl) / p.num_k_blocks == ts) ? 0 : 1;
                     const size_t part = (static_cast<size_t>(sl * 2 + piece) * CTAS + rank) * S::PARTIAL_FLOATS;
-                    float4 x[16];
+                    float4 x[EC / 4];
 #pragma unroll
-                    for (int h = 0; h < 2; ++h) {
+                    for (int h = 0; h < EC / 32; ++h) {
 #pragma unroll
                         for (int j = 0; j < 8; ++j) {
                             x[8 * h + j] = __ldcg(reinterpret_cast<const float4*>(
-                                part_base + part + partial_offset<BN>(quad, 2 * c + h, j, lane)));
+                                part_base + part + partial_offset<BN>(quad, (EC / 32) * c + h, j, lane)));
                         }
                     }
 #pragma unroll
-                    for (int j = 0; j < 16; ++j) {
+                    for (int j = 0; j < EC / 4; ++j) {
                         v[4 * j + 0] += x[j].x;
                         v[4 * j + 1] += x[j].y;
                         v[4 * j + 2] += x[j].z;
                         v[4 * j + 3] += x[j].w;
                     }
                 }
-                store_chunk(v, row0, nb * BN + c * 64);
+                store_chunk(v, row0, nb * BN + c * EC);
             }
             release_accumulator();
             if (epi_tid == 0) *counter = 0;  // leave the workspace ready for the next call

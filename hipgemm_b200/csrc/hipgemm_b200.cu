@@ -55,6 +55,7 @@ struct KernelConfig {
     double eff;      // relative per-SM throughput at large sizes (measured), for the choice
     int smem_bytes;
     int partial_floats;  // one CTA's fp32 partial tile (stream-K workspace unit)
+    int epi_cols;        // columns per C store box (64: 128-byte swizzle, 32: 64-byte swizzle)
     const void* kernel;  // __global__ function pointer
     int (*launch)(const CUtensorMap&, const CUtensorMap&, const CUtensorMap&, const GemmParams&,
                   const PeerOutputs&, int grid, cudaStream_t);
@@ -87,17 +88,19 @@ KernelConfig make_config(const char* name, double eff) {
                         S::BM,        BN,
                         S::B_ROWS,    eff,
                         S::SMEM_BYTES, S::PARTIAL_FLOATS,
+                        S::EPI_COLS,
                         reinterpret_cast<const void*>(&fp8_gemm_tn_sm100<CTAS, BN, STAGES>),
                         &launch_kernel<CTAS, BN, STAGES>};
 }
 
 const KernelConfig kConfigs[] = {
-    {"auto", 0, 0, 0, 0, 0.0, 0, 0, nullptr, nullptr},
+    {"auto", 0, 0, 0, 0, 0.0, 0, 0, 0, nullptr, nullptr},
     make_config<1, 256, 4>("bn256_s4", 0.93),
     make_config<1, 128, 6>("bn128_s6", 0.70),
     make_config<1, 64, 8>("bn64_s8", 0.35),
     make_config<2, 256, 6>("pair256_s6", 1.0),
     make_config<2, 128, 8>("pair128_s8", 0.62),
+    make_config<2, 224, 6>("pair224_s6", 0.90),
 };
 constexpr int kNumConfigs = sizeof(kConfigs) / sizeof(kConfigs[0]);
 
@@ -188,13 +191,14 @@ const DeviceState* current_device_setup(int* rc) {
 }
 
 bool encode_2d(CUtensorMap* map, CUtensorMapDataType dtype, size_t elem_bytes, const void* ptr, uint64_t inner,
-               uint64_t outer, uint32_t box_inner, uint32_t box_outer) {
+               uint64_t outer, uint32_t box_inner, uint32_t box_outer,
+               CUtensorMapSwizzle swizzle = CU_TENSOR_MAP_SWIZZLE_128B) {
     const cuuint64_t dims[2] = {inner, outer};
     const cuuint64_t strides[1] = {inner * elem_bytes};
     const cuuint32_t box[2] = {box_inner, box_outer};
     const cuuint32_t estr[2] = {1, 1};
     return g_encode(map, dtype, 2, const_cast<void*>(ptr), dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
-                    CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                    swizzle, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
                     CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
 }
 
@@ -318,20 +322,21 @@ int run_gemm(const void* A, const void* B, void* C, int M, int N, int K, const f
     const KernelConfig& kc = kConfigs[c];
     const Schedule sc = make_schedule(M, N, K, c, schedule, *dev);
 
+    const CUtensorMapSwizzle c_swizzle = kc.epi_cols == 64 ? CU_TENSOR_MAP_SWIZZLE_128B : CU_TENSOR_MAP_SWIZZLE_64B;
     CUtensorMap ta, tb, tc;
     if (!encode_2d(&ta, CU_TENSOR_MAP_DATA_TYPE_UINT8, 1, A, static_cast<uint64_t>(K), static_cast<uint64_t>(M), 128,
                    128) ||
         !encode_2d(&tb, CU_TENSOR_MAP_DATA_TYPE_UINT8, 1, B, static_cast<uint64_t>(K), static_cast<uint64_t>(N), 128,
                    static_cast<uint32_t>(kc.b_box_rows)) ||
-        !encode_2d(&tc, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, C, static_cast<uint64_t>(N), static_cast<uint64_t>(M), 64,
-                   32)) {
+        !encode_2d(&tc, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, C, static_cast<uint64_t>(N), static_cast<uint64_t>(M),
+                   static_cast<uint32_t>(kc.epi_cols), 32, c_swizzle)) {
         return HGEMM_ERR_CUDA;
     }
     PeerOutputs peers{};
     if (n_peer < 0 || n_peer > kMaxPeerOutputs) return HGEMM_ERR_INVALID_VALUE;
     for (int i = 0; i < n_peer; ++i) {
         if (!encode_2d(&peers.maps[i], CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, peer_c[i], static_cast<uint64_t>(N),
-                       static_cast<uint64_t>(M), 64, 32)) {
+                       static_cast<uint64_t>(M), static_cast<uint32_t>(kc.epi_cols), 32, c_swizzle)) {
             return HGEMM_ERR_CUDA;
         }
     }

@@ -74,7 +74,7 @@ def test_ragged_tails(cuda_device, M, N, K):
     _run(M, N, K, seed_a=M, seed_b=N + K)
 
 
-@pytest.mark.parametrize("config", [1, 2, 3, 4, 5])
+@pytest.mark.parametrize("config", [1, 2, 3, 4, 5, 6])
 @pytest.mark.parametrize("M,N,K", [(391, 648, 784), (1000, 1032, 2064), (2048, 2048, 1024)])
 def test_every_tile_config(cuda_device, config, M, N, K):
     _run(M, N, K, config=config)
@@ -151,7 +151,7 @@ def test_against_cublaslt_scaled_mm(cuda_device):
     assert oracle.validate(c_bits(lt), ref)[0] == 0
 
 
-@pytest.mark.parametrize("config", [1, 2, 3, 4, 5])
+@pytest.mark.parametrize("config", [1, 2, 3, 4, 5, 6])
 @pytest.mark.parametrize("M,N,K", [(1000, 1032, 2064), (391, 648, 784), (128, 2048, 4096), (4000, 1024, 1152)])
 def test_stream_k_schedule(cuda_device, config, M, N, K):
     """Forced stream-K: partial tiles reduced by their last contributor match the oracle."""

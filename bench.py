@@ -80,6 +80,15 @@ def fp8_peak_tflops() -> tuple[float, str]:
         return 2.0 * 1590.0, "fallback (2 x 1590 TFLOP/s bf16)"
 
 
+def hbm_peak_gbs() -> tuple[float, str]:
+    """Measured HBM copy bandwidth from MEASURED_PEAKS.json, else the pool's fallback."""
+    try:
+        with open(os.path.join(ROOT, "MEASURED_PEAKS.json")) as f:
+            return float(json.load(f)["hbm_gbs"]), "measured (hbm_gbs of MEASURED_PEAKS.json)"
+    except Exception:
+        return 6650.0, "fallback (6.65 TB/s)"
+
+
 _REASONS = [
     (0x1, "gpu_idle"), (0x2, "applications_clocks_setting"), (0x4, "sw_power_cap"), (0x8, "hw_slowdown"),
     (0x10, "sync_boost"), (0x20, "sw_thermal_slowdown"), (0x40, "hw_thermal_slowdown"),
@@ -318,6 +327,20 @@ def run_ours(args) -> None:
         ms_lt, _ = timed(lt_step, args.steps, max(3, args.warmup))
         extra["cublaslt_fp8"] = {"value": flops_total / (ms_lt * 1e-3) / 1e12, "unit": "TFLOP/s",
                                  "ms_per_step": ms_lt, "what": "torch._scaled_mm (cuBLASLt), same inputs"}
+
+    # The device quantiser on this rank's A-shaped fp32 activations (HBM-bound; inputs > L2).
+    xq = torch.randn((m, K), device=dev, dtype=torch.float32)
+    qq = torch.empty((m, K), dtype=torch.uint8, device=dev)
+    sq = torch.empty(1, dtype=torch.float32, device=dev)
+    ms_q, _ = timed(lambda i: hg.quantize_e4m3(xq, out=qq, scale=sq), max(5, min(args.steps, 50)), 3)
+    hbm_peak = hbm_peak_gbs()
+    q_bytes = 5.0 * m * K  # algorithmic: read fp32 x once, write e4m3 q once
+    extra["quantizer"] = {
+        "what": "hgemm_quantize_e4m3 fp32 -> e4m3, per-tensor amax/448, on this rank's A shape",
+        "ms_per_call": ms_q, "achieved_gbs": q_bytes / (ms_q * 1e-3) / 1e9, "peak_gbs": hbm_peak[0],
+        "frac": q_bytes / (ms_q * 1e-3) / 1e9 / hbm_peak[0], "peak_source": hbm_peak[1],
+        "algorithmic_bytes": q_bytes, "moved_bytes": 9.0 * m * K}
+    del xq, qq
 
     # End to end through the public API: pinned host A/B in, GEMM, C back to pinned host.
     hA = A[0].cpu().pin_memory()

@@ -22,6 +22,9 @@ HGEMM_SCHEDULE_AUTO = 0
 HGEMM_SCHEDULE_DATA_PARALLEL = 1
 HGEMM_SCHEDULE_STREAM_K = 2
 
+HGEMM_DTYPE_F32 = 0
+HGEMM_DTYPE_BF16 = 1
+
 
 class HgemmError(RuntimeError):
     """A negative status code from the C ABI (never a silent fallback)."""
@@ -50,6 +53,7 @@ _SIGNATURES = {
     "hgemm_ipc_export": (_i, [_vp, _vp, ctypes.POINTER(ctypes.c_size_t)]),
     "hgemm_ipc_import": (_i, [_vp, ctypes.POINTER(ctypes.c_void_p)]),
     "hgemm_ipc_close": (_i, [_vp]),
+    "hgemm_quantize_e4m3": (_i, [_vp, _i, ctypes.c_size_t, _vp, _vp, _vp]),
     "hgemm_num_configs": (_i, []),
     "hgemm_config_resident_ctas": (_i, [_i]),
     "hgemm_config_name": (ctypes.c_char_p, [_i]),

@@ -133,3 +133,29 @@ def host_make_quantized(n: int, seed: int, mean: float = 0.0, stddev: float = 1.
         out = torch.empty(n, dtype=torch.uint8)
     scale = lib().hgemm_host_make_quantized(out.data_ptr(), n, seed, mean, stddev)
     return out, float(scale)
+
+
+def quantize_e4m3(x: torch.Tensor, out: torch.Tensor | None = None, scale: torch.Tensor | None = None,
+                  stream: torch.cuda.Stream | None = None) -> tuple[torch.Tensor, torch.Tensor]:
+    """Per-tensor e4m3 quantisation on the GPU (hgemm_quantize_e4m3): returns (q, scale)
+    with scale = amax(|x|)/448 as a 1-element float32 tensor and q = e4m3(x / scale) as
+    uint8 bits of x's shape, ready for fp8_gemm_tn."""
+    if not x.is_cuda or not x.is_contiguous():
+        raise ValueError("x must be a contiguous CUDA tensor (there is no CPU path)")
+    if x.dtype == torch.float32:
+        dt = 0
+    elif x.dtype == torch.bfloat16:
+        dt = 1
+    else:
+        raise TypeError(f"x must be float32 or bfloat16, got {x.dtype}")
+    if out is None:
+        out = torch.empty(x.shape, dtype=torch.uint8, device=x.device)
+    if scale is None:
+        scale = torch.empty(1, dtype=torch.float32, device=x.device)
+    if out.numel() != x.numel() or out.dtype != torch.uint8 or not out.is_contiguous():
+        raise ValueError("out must be a contiguous uint8 tensor with x's size")
+    with torch.cuda.device(x.device):
+        rc = lib().hgemm_quantize_e4m3(x.data_ptr(), dt, x.numel(), out.data_ptr(), scale.data_ptr(),
+                                       _stream_handle(stream))
+    check(rc, "hgemm_quantize_e4m3")
+    return out, scale

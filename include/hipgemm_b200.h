@@ -157,6 +157,21 @@ const char* hgemm_error_string(int code);
 /* Library version string. */
 const char* hgemm_version(void);
 
+/* ---- device quantiser ------------------------------------------------------------------- */
+
+#define HGEMM_DTYPE_F32 0
+#define HGEMM_DTYPE_BF16 1
+
+/* Per-tensor e4m3 quantisation on the device, stream-ordered: *d_scale = amax(|x|) / 448
+ * (1.0 for an all-zero tensor; NaN elements are ignored) and q[i] = e4m3(x[i] / scale),
+ * IEEE division, round-to-nearest-even, saturating to +-448.  x: n fp32 or bf16 values
+ * (x_dtype), q: n bytes, both 16-byte aligned; d_scale: one float of device memory (used
+ * as the amax accumulator until the last step writes the scale).  The result feeds
+ * hgemm_fp8_tn directly (q as A or B, d_scale as its scale).  The reference quantises on
+ * the host without a scale (utils.hpp:27-33); this is the benchmark configs' amax/448
+ * quantiser moved onto the GPU. */
+int hgemm_quantize_e4m3(const void* x, int x_dtype, size_t n, void* q, float* d_scale, hgemm_stream_t stream);
+
 /* ---- host utilities mirroring the reference harness (utils.hpp) ---------------------- */
 
 /* utils.hpp:27-33 init_random, generalised: std::mt19937(seed) feeding

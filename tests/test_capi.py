@@ -123,3 +123,13 @@ def test_fused_allgather_and_ipc_argument_checks():
     assert L.hgemm_ipc_export(None, None, None) == hg.HGEMM_ERR_INVALID_VALUE
     assert L.hgemm_ipc_import(None, None) == hg.HGEMM_ERR_INVALID_VALUE
     assert L.hgemm_ipc_close(None) == hg.HGEMM_ERR_INVALID_VALUE
+
+
+def test_quantiser_argument_checks():
+    L = hg.lib()
+    assert L.hgemm_quantize_e4m3(FAKE, 0, 16, FAKE, None, None) == hg.HGEMM_ERR_INVALID_VALUE
+    assert L.hgemm_quantize_e4m3(None, 0, 16, FAKE, FAKE, None) == hg.HGEMM_ERR_INVALID_VALUE
+    assert L.hgemm_quantize_e4m3(FAKE, 2, 16, FAKE, FAKE, None) == hg.HGEMM_ERR_INVALID_VALUE
+    assert L.hgemm_quantize_e4m3(FAKE + 4, 0, 16, FAKE, FAKE, None) == hg.HGEMM_ERR_ALIGNMENT
+    assert L.hgemm_quantize_e4m3(FAKE, 1, 16, FAKE + 8, FAKE, None) == hg.HGEMM_ERR_ALIGNMENT
+    assert L.hgemm_quantize_e4m3(FAKE, 0, 16, FAKE, FAKE + 2, None) == hg.HGEMM_ERR_ALIGNMENT

@@ -46,7 +46,7 @@ METRIC = "FP8 e4m3 GEMM TFLOP/s and % of dense FP8 peak"
 # DRAM bytes (read + write) of one launch of the GEMM kernel, from an ncu capture of
 # the same workload (see profiles/); keyed by (workload, gpus).  None = not captured.
 TRAFFIC_BYTES_PER_LAUNCH: dict[tuple[str, int], float] = {
-    ("8192", 1): 344.333e6 + 116.975e6,  # profiles/fp8_gemm_tn_8192_pair256.md (pair<256, 6>)
+    ("8192", 1): 345.692e6 + 117.302e6,  # profiles/fp8_gemm_tn_8192_pair256.md (<2, 256, 6>, current build)
 }
 
 

@@ -352,15 +352,13 @@ def run_ours(args) -> None:
     dS = torch.empty(2, dtype=torch.float32, device=dev)
 
     def e2e_step(i):
-        dA.copy_(hA, non_blocking=True)
-        dB.copy_(hB, non_blocking=True)
-        dS.copy_(hS, non_blocking=True)
-        sg.run(dA, dB, dS[0:1], dS[1:2], out=C, config=config)
-        hC.copy_(C, non_blocking=True)
+        # Public host-buffer API: A, B and the scales copied in, C copied out, with the
+        # copies overlapped with the per-block GEMMs inside the call.
+        hg.fp8_gemm_tn_from_host(hA, hB, hC, hS, dA, dB, C, dS)
 
     e2e_steps = max(1, min(args.steps, 50))
     ms_e2e, _ = timed(e2e_step, e2e_steps, 2)
-    e2e = {"value": flops_total / (ms_e2e * 1e-3) / 1e12, "unit": "TFLOP/s",
+    e2e = {"value": flops_total / (ms_e2e * 1e-3) / 1e12, "unit": "TFLOP/s", "api": "hgemm_fp8_tn_from_host",
            "h2d_bytes_per_step": int(hA.numel() + hB.numel() + 4 * hS.numel()),
            "d2h_bytes_per_step": int(2 * hC.numel()), "steps": e2e_steps, "ms_per_step": ms_e2e}
 

@@ -159,3 +159,29 @@ def quantize_e4m3(x: torch.Tensor, out: torch.Tensor | None = None, scale: torch
                                        _stream_handle(stream))
     check(rc, "hgemm_quantize_e4m3")
     return out, scale
+
+
+def fp8_gemm_tn_from_host(a_host: torch.Tensor, b_host: torch.Tensor, c_host: torch.Tensor,
+                          scales_host: torch.Tensor | None, d_a: torch.Tensor, d_b: torch.Tensor, d_c: torch.Tensor,
+                          d_scales: torch.Tensor | None = None, stream: torch.cuda.Stream | None = None) -> torch.Tensor:
+    """C = sa*sb * A . B^T from host tensors into a host tensor, with the copies in and out
+    overlapped with the GEMMs (hgemm_fp8_tn_from_host).  a_host (M, K) and b_host (N, K)
+    uint8 e4m3 bits, c_host (M, N) bfloat16, scales_host 2 float32 (or None) -- all on
+    the CPU, ideally pinned; d_a, d_b, d_c, d_scales: device buffers of the same shapes."""
+    M, K = a_host.shape
+    N = b_host.shape[0]
+    for name, t in (("a_host", a_host), ("b_host", b_host), ("c_host", c_host)):
+        if t.is_cuda or not t.is_contiguous():
+            raise ValueError(f"{name} must be a contiguous CPU tensor")
+    if c_host.dtype != torch.bfloat16 or tuple(c_host.shape) != (M, N):
+        raise ValueError("c_host must be an (M, N) bfloat16 tensor")
+    if tuple(d_c.shape) != (M, N) or d_c.dtype != torch.bfloat16:
+        raise ValueError("d_c must be an (M, N) bfloat16 CUDA tensor")
+    if scales_host is not None and (scales_host.numel() != 2 or scales_host.dtype != torch.float32 or d_scales is None):
+        raise ValueError("scales_host must hold 2 float32 values, with a 2-float d_scales")
+    with torch.cuda.device(d_c.device):
+        rc = lib().hgemm_fp8_tn_from_host(a_host.data_ptr(), b_host.data_ptr(), c_host.data_ptr(), M, N, K,
+                                          _ptr(scales_host), d_a.data_ptr(), d_b.data_ptr(), d_c.data_ptr(),
+                                          _ptr(d_scales), _stream_handle(stream))
+    check(rc, "hgemm_fp8_tn_from_host")
+    return c_host

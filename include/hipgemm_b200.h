@@ -60,6 +60,20 @@ int hgemm_fp8_tn(const void* A, const void* B, void* C, int M, int N, int K, con
 int hgemm_fp8_tn_rows(const void* A, const void* B, void* C, int M, int N, int K, int row_begin, int row_end,
                       const float* d_scale_a, const float* d_scale_b, hgemm_stream_t stream);
 
+/* The whole product from host buffers, as the reference's test.cpp:73-81 does it (copy A
+ * and B in, launch, copy C out), pipelined: A and B go to the device in up to 4 row
+ * panels each, alternately, on one internal stream; each of the up-to 4 x 4 C blocks is
+ * computed on a second stream as soon as its A and B panels have arrived, and copied back
+ * to C_host on a third as soon as it is done, so both copy directions and the GEMMs
+ * overlap.  Host buffers should be pinned (cudaMallocHost) for the copies to be
+ * asynchronous.  d_A (M x K), d_B (N x K), d_C (M x N bf16) and d_scales (2 floats) are
+ * caller-owned device buffers; h_scales (2 host floats: scale_a, scale_b) or NULL for 1.0.
+ * Stream-ordered with respect to `stream` at both ends; host buffers must stay valid
+ * until that stream reaches this point.  No counterpart in the reference. */
+int hgemm_fp8_tn_from_host(const void* A_host, const void* B_host, void* C_host, int M, int N, int K,
+                           const float* h_scales, void* d_A, void* d_B, void* d_C, float* d_scales,
+                           hgemm_stream_t stream);
+
 /* The M-sharded call fused with the all-gather of C.  C_ranks[i] is rank i's full M x N
  * C buffer as mapped into this process (C_ranks[rank] is this GPU's own; the others are
  * peer memory opened with hgemm_ipc_import, 1 <= nranks <= 8).  Rows [row_begin, row_end)

@@ -133,3 +133,14 @@ def test_quantiser_argument_checks():
     assert L.hgemm_quantize_e4m3(FAKE + 4, 0, 16, FAKE, FAKE, None) == hg.HGEMM_ERR_ALIGNMENT
     assert L.hgemm_quantize_e4m3(FAKE, 1, 16, FAKE + 8, FAKE, None) == hg.HGEMM_ERR_ALIGNMENT
     assert L.hgemm_quantize_e4m3(FAKE, 0, 16, FAKE, FAKE + 2, None) == hg.HGEMM_ERR_ALIGNMENT
+
+
+def test_from_host_argument_checks():
+    L = hg.lib()
+    args = (FAKE, FAKE, FAKE)
+    assert L.hgemm_fp8_tn_from_host(*args, -1, 8, 16, None, FAKE, FAKE, FAKE, None, None) == hg.HGEMM_ERR_INVALID_VALUE
+    assert L.hgemm_fp8_tn_from_host(FAKE, FAKE, None, 8, 8, 16, None, FAKE, FAKE, FAKE, None, None) == \
+        hg.HGEMM_ERR_INVALID_VALUE
+    assert L.hgemm_fp8_tn_from_host(*args, 8, 8, 24, None, FAKE, FAKE, FAKE, None, None) == hg.HGEMM_ERR_ALIGNMENT
+    assert L.hgemm_fp8_tn_from_host(*args, 8, 8, 16, FAKE, FAKE, FAKE, FAKE, None, None) == hg.HGEMM_ERR_INVALID_VALUE
+    assert L.hgemm_fp8_tn_from_host(*args, 0, 8, 16, None, None, None, None, None, None) == hg.HGEMM_OK

@@ -55,6 +55,9 @@ _SIGNATURES = {
     "hgemm_ipc_close": (_i, [_vp]),
     "hgemm_quantize_e4m3": (_i, [_vp, _i, ctypes.c_size_t, _vp, _vp, _vp]),
     "hgemm_fp8_tn_from_host": (_i, [_vp, _vp, _vp, _i, _i, _i, _vp, _vp, _vp, _vp, _vp, _vp]),
+    "hgemm_fp8_tn_mx": (_i, [_vp, _vp, _vp, _i, _i, _i, _vp, _vp, _vp, _vp, _vp]),
+    "hgemm_mx_sf_bytes": (ctypes.c_size_t, [_i, _i]),
+    "hgemm_host_mx_sf_to_blocked": (_i, [_vp, _i, _i, _vp]),
     "hgemm_num_configs": (_i, []),
     "hgemm_config_resident_ctas": (_i, [_i]),
     "hgemm_config_name": (ctypes.c_char_p, [_i]),

@@ -61,6 +61,12 @@ struct GemmParams {
     int sk_slots;
     float* partials;  // [slot][piece 0/1][cta][128 x BN] fp32 (layout: partial_offset)
     int* counters;    // [sk tile][cta]; zero on entry, left zero on exit
+    // MX block scaling (the MX kernel only): e8m0 scale factors, one per 32 K elements of a
+    // row, in 512-byte atoms of 128 rows x 4 K-groups (byte 16*(r%32) + 4*(r/32) + g),
+    // atom (row block i, K block j) at offset (i * sf_k_atoms + j) * 512.
+    const uint8_t* sfa;
+    const uint8_t* sfb;
+    int sf_k_atoms;
 };
 
 // Extra outputs for the fused all-gather: the same C rows on other GPUs (peer memory
@@ -198,7 +204,7 @@ __device__ __forceinline__ void st_global_v4(float* p, float a, float b, float c
     asm volatile("st.global.v4.f32 [%0], {%1, %2, %3, %4};" ::"l"(p), "f"(a), "f"(b), "f"(c), "f"(d) : "memory");
 }
 
-template <int CTAS, int BN, int STAGES>
+template <int CTAS, int BN, int STAGES, bool MX = false>
 struct KernelShape {
     static constexpr int BM = 128 * CTAS;   // output tile rows
     static constexpr int BK = 128;          // bytes of K per stage = one 128-byte swizzle row
@@ -215,16 +221,25 @@ struct KernelShape {
     static constexpr int OFF_A = 0;
     static constexpr int OFF_B = OFF_A + STAGES * A_BYTES;
     static constexpr int OFF_EPI = OFF_B + STAGES * B_BYTES;
-    static constexpr int OFF_BAR = OFF_EPI + 4 * 2 * EPI_BUF_BYTES;
+    // MX: per stage, one 512-byte scale-factor atom for A's 128 rows and one per 128 rows of B.
+    static constexpr int SFB_ATOMS = (BN + 127) / 128;
+    static constexpr int SF_BYTES = MX ? 512 * (1 + SFB_ATOMS) : 0;
+    static constexpr int OFF_SF = OFF_EPI + 4 * 2 * EPI_BUF_BYTES;
+    static constexpr int OFF_BAR = OFF_SF + STAGES * SF_BYTES;
     static constexpr int NUM_BARS = 2 * STAGES + 5;  // full, empty, tfull x2, tempty x2, drain
     static constexpr int OFF_MISC = OFF_BAR + NUM_BARS * 8;
     static constexpr int SMEM_BYTES = OFF_MISC + 16 + 1024;  // + slack to align the base to 1024 B
-    // Two accumulators of BN fp32 columns, rounded up to the power of two tcgen05.alloc takes.
+    // Two accumulators of BN fp32 columns, plus (MX) per-stage scale-factor columns (4 per
+    // 128 rows of A and of B), rounded up to the power of two tcgen05.alloc takes.
+    static constexpr int SF_COLS = MX ? 4 * (1 + SFB_ATOMS) : 0;
+    static constexpr int COLS_USED = 2 * BN + STAGES * SF_COLS;
     static constexpr uint32_t TMEM_COLS =
-        2 * BN <= 32 ? 32 : (2 * BN <= 64 ? 64 : (2 * BN <= 128 ? 128 : (2 * BN <= 256 ? 256 : 512)));
+        COLS_USED <= 32 ? 32 : (COLS_USED <= 64 ? 64 : (COLS_USED <= 128 ? 128 : (COLS_USED <= 256 ? 256 : 512)));
     static constexpr uint32_t IDESC = idesc_e4m3_f32(BM, BN);
     static constexpr int PARTIAL_FLOATS = 128 * BN;  // one CTA's share of a partial tile
     static_assert(CTAS == 1 || CTAS == 2, "one CTA or a CTA pair");
+    static_assert(!MX || CTAS == 1, "MX block scaling is built for the single-CTA tile");
+    static_assert(COLS_USED <= 512, "tensor memory holds 512 columns");
     static_assert(BN % 32 == 0 && BN >= 64 && BN <= 256, "BN must be a multiple of 32 in [64, 256]");
     static_assert(CTAS == 1 || BN % 16 == 0, "M=256 MMAs need N % 16 == 0");
     static_assert(B_BYTES % 1024 == 0, "B tiles must keep 1024-byte alignment");
@@ -232,12 +247,12 @@ struct KernelShape {
     static_assert(SMEM_BYTES <= 232448, "exceeds 227 KB of shared memory per CTA");
 };
 
-template <int CTAS, int BN, int STAGES>
+template <int CTAS, int BN, int STAGES, bool MX = false>
 __global__ void __launch_bounds__(192, 1)
     fp8_gemm_tn_sm100(const __grid_constant__ CUtensorMap tm_a, const __grid_constant__ CUtensorMap tm_b,
                       const __grid_constant__ CUtensorMap tm_c, const GemmParams p,
                       const __grid_constant__ PeerOutputs peers) {
-    using S = KernelShape<CTAS, BN, STAGES>;
+    using S = KernelShape<CTAS, BN, STAGES, MX>;
     extern __shared__ uint8_t smem_raw[];
     // 128-byte swizzle atoms need 1024-byte alignment.
     const uint32_t raw_base = smem_u32(smem_raw);
@@ -320,9 +335,21 @@ __global__ void __launch_bounds__(192, 1)
                         // For a pair: the MMAs that read this stage finished in both CTAs.
                         if (kPair && !first_pass) mbar_arrive_cluster(peer_empty0 + 8 * stage);
                         const uint32_t full = bar_full + 8 * stage;
-                        mbar_arrive_expect_tx(full, CTAS * S::STAGE_BYTES);
+                        mbar_arrive_expect_tx(full, CTAS * S::STAGE_BYTES + S::SF_BYTES);
                         tma_load_2d(a_dst, &tm_a, kb * S::BK, a_row, full);
                         tma_load_2d(b_dst, &tm_b, kb * S::BK, b_row, full);
+                        if constexpr (MX) {
+                            // This K block's scale-factor atoms: A's row block mb, B's
+                            // 128-row blocks of column block nb.
+                            const uint32_t sf_dst = base + S::OFF_SF + stage * S::SF_BYTES;
+                            const size_t ka = static_cast<size_t>(p.sf_k_atoms);
+                            bulk_load_1d(sf_dst, p.sfa + (static_cast<size_t>(mb) * ka + kb) * 512, 512, full);
+#pragma unroll
+                            for (int i = 0; i < S::SFB_ATOMS; ++i) {
+                                const size_t rb = static_cast<size_t>(nb) * S::SFB_ATOMS + i;
+                                bulk_load_1d(sf_dst + 512 * (1 + i), p.sfb + (rb * ka + kb) * 512, 512, full);
+                            }
+                        }
                     } else {
                         const uint32_t full = full_leader0 + 8 * stage;
                         tma_load_2d_pair(a_dst, &tm_a, kb * S::BK, a_row, full);
@@ -362,13 +389,35 @@ __global__ void __launch_bounds__(192, 1)
                     tc_fence_after();
                     const uint64_t a_desc = sw128_kmajor_desc(base + S::OFF_A + stage * S::A_BYTES);
                     const uint64_t b_desc = sw128_kmajor_desc(base + S::OFF_B + stage * S::B_BYTES);
+                    if constexpr (MX) {
+                        // Scale factors of this stage into its tensor-memory columns: A's at
+                        // tsfa (4 columns), B's after them; the MMAs below read them in order.
+                        const uint32_t tsfa = tmem_base + static_cast<uint32_t>(2 * BN + stage * S::SF_COLS);
+                        const uint32_t tsfb = tsfa + 4;
+                        const uint32_t sf_src = base + S::OFF_SF + stage * S::SF_BYTES;
+                        tmem_cp_32x128b_warpx4(tsfa, sf_smem_desc(sf_src));
 #pragma unroll
-                    for (int k = 0; k < S::BK / S::UMMA_K; ++k) {
-                        // Advancing the start address by 32 B walks K inside the swizzle
-                        // atom: the hardware applies the XOR pattern to the final address.
-                        const uint64_t koff = static_cast<uint64_t>((k * S::UMMA_K) >> 4);
-                        const uint32_t accumulate = (kb > w.kb_begin || k > 0) ? 1u : 0u;
-                        mma_f8f6f4<CTAS>(d_tmem, a_desc + koff, b_desc + koff, S::IDESC, accumulate);
+                        for (int i = 0; i < S::SFB_ATOMS; ++i) {
+                            tmem_cp_32x128b_warpx4(tsfb + 4 * i, sf_smem_desc(sf_src + 512 * (1 + i)));
+                        }
+#pragma unroll
+                        for (int k = 0; k < S::BK / S::UMMA_K; ++k) {
+                            const uint64_t koff = static_cast<uint64_t>((k * S::UMMA_K) >> 4);
+                            const uint32_t accumulate = (kb > w.kb_begin || k > 0) ? 1u : 0u;
+                            // K slice k uses byte k of each scale-factor column.
+                            const uint32_t sf_id = static_cast<uint32_t>(k);
+                            mma_mxf8f6f4(d_tmem, a_desc + koff, b_desc + koff, idesc_mx_e4m3(S::BM, BN, sf_id),
+                                         tsfa | (sf_id << 30), tsfb | (sf_id << 30), accumulate);
+                        }
+                    } else {
+#pragma unroll
+                        for (int k = 0; k < S::BK / S::UMMA_K; ++k) {
+                            // Advancing the start address by 32 B walks K inside the swizzle
+                            // atom: the hardware applies the XOR pattern to the final address.
+                            const uint64_t koff = static_cast<uint64_t>((k * S::UMMA_K) >> 4);
+                            const uint32_t accumulate = (kb > w.kb_begin || k > 0) ? 1u : 0u;
+                            mma_f8f6f4<CTAS>(d_tmem, a_desc + koff, b_desc + koff, S::IDESC, accumulate);
+                        }
                     }
                     mma_commit<CTAS>(bar_empty + 8 * stage);  // frees the stage when these MMAs finish
                     if (++stage == STAGES) {

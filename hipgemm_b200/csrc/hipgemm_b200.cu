@@ -61,10 +61,10 @@ struct KernelConfig {
                   const PeerOutputs&, int grid, cudaStream_t);
 };
 
-template <int CTAS, int BN, int STAGES>
+template <int CTAS, int BN, int STAGES, bool MX = false>
 int launch_kernel(const CUtensorMap& ta, const CUtensorMap& tb, const CUtensorMap& tc, const GemmParams& p,
                   const PeerOutputs& peers, int grid, cudaStream_t stream) {
-    using S = KernelShape<CTAS, BN, STAGES>;
+    using S = KernelShape<CTAS, BN, STAGES, MX>;
     cudaLaunchConfig_t cfg{};
     cfg.gridDim = dim3(static_cast<unsigned>(grid), 1, 1);
     cfg.blockDim = dim3(S::kNumThreads, 1, 1);
@@ -77,20 +77,20 @@ int launch_kernel(const CUtensorMap& ta, const CUtensorMap& tb, const CUtensorMa
     attr[0].val.clusterDim.z = 1;
     cfg.attrs = attr;
     cfg.numAttrs = CTAS == 2 ? 1 : 0;
-    const cudaError_t e = cudaLaunchKernelEx(&cfg, fp8_gemm_tn_sm100<CTAS, BN, STAGES>, ta, tb, tc, p, peers);
+    const cudaError_t e = cudaLaunchKernelEx(&cfg, fp8_gemm_tn_sm100<CTAS, BN, STAGES, MX>, ta, tb, tc, p, peers);
     return e == cudaSuccess ? HGEMM_OK : HGEMM_ERR_CUDA;
 }
 
-template <int CTAS, int BN, int STAGES>
+template <int CTAS, int BN, int STAGES, bool MX = false>
 KernelConfig make_config(const char* name, double eff) {
-    using S = KernelShape<CTAS, BN, STAGES>;
+    using S = KernelShape<CTAS, BN, STAGES, MX>;
     return KernelConfig{name,         CTAS,
                         S::BM,        BN,
                         S::B_ROWS,    eff,
                         S::SMEM_BYTES, S::PARTIAL_FLOATS,
                         S::EPI_COLS,
-                        reinterpret_cast<const void*>(&fp8_gemm_tn_sm100<CTAS, BN, STAGES>),
-                        &launch_kernel<CTAS, BN, STAGES>};
+                        reinterpret_cast<const void*>(&fp8_gemm_tn_sm100<CTAS, BN, STAGES, MX>),
+                        &launch_kernel<CTAS, BN, STAGES, MX>};
 }
 
 const KernelConfig kConfigs[] = {
@@ -103,6 +103,9 @@ const KernelConfig kConfigs[] = {
     make_config<2, 224, 6>("pair224_s6", 0.90),
 };
 constexpr int kNumConfigs = sizeof(kConfigs) / sizeof(kConfigs[0]);
+
+// MX block-scaled kernel: 128 x 128 tiles, 5 stages (the scale-factor atoms take the sixth).
+const KernelConfig kMxConfig = make_config<1, 128, 5, true>("mx_bn128_s5", 1.0);
 
 void init_encode() {
     void* fn = nullptr;
@@ -160,6 +163,11 @@ int device_setup(int dev) {
                 return;
             }
             st.resident_ctas[c] = clusters * k.ctas;
+        }
+        if (cudaFuncSetAttribute(kMxConfig.kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                 kMxConfig.smem_bytes) != cudaSuccess) {
+            st.status = HGEMM_ERR_CUDA;
+            return;
         }
         // Library-owned stream-ordered pool for stream-K workspaces; it keeps its memory
         // (release threshold = max) so repeated calls do not map pages again.
@@ -378,10 +386,79 @@ int run_gemm(const void* A, const void* B, void* C, int M, int N, int K, const f
     return rc;
 }
 
+int run_gemm_mx(const void* A, const void* B, void* C, int M, int N, int K, const void* sfa, const void* sfb,
+                const float* sa, const float* sb, cudaStream_t stream) {
+    int rc = check_args(A, B, C, M, N, K, 0, HGEMM_SCHEDULE_DATA_PARALLEL);
+    if (rc != HGEMM_OK || M == 0 || N == 0) return rc;
+    if (K % 32 != 0) return HGEMM_ERR_ALIGNMENT;
+    if (K > 0 && (!sfa || !sfb)) return HGEMM_ERR_INVALID_VALUE;
+    if ((reinterpret_cast<uintptr_t>(sfa) & 15u) || (reinterpret_cast<uintptr_t>(sfb) & 15u)) return HGEMM_ERR_ALIGNMENT;
+    const DeviceState* dev = current_device_setup(&rc);
+    if (rc != HGEMM_OK) return rc;
+    if (K == 0) {
+        return cudaMemsetAsync(C, 0, static_cast<size_t>(M) * N * 2, stream) == cudaSuccess ? HGEMM_OK
+                                                                                              : HGEMM_ERR_CUDA;
+    }
+    const KernelConfig& kc = kMxConfig;
+    CUtensorMap ta, tb, tc;
+    if (!encode_2d(&ta, CU_TENSOR_MAP_DATA_TYPE_UINT8, 1, A, static_cast<uint64_t>(K), static_cast<uint64_t>(M), 128,
+                   128) ||
+        !encode_2d(&tb, CU_TENSOR_MAP_DATA_TYPE_UINT8, 1, B, static_cast<uint64_t>(K), static_cast<uint64_t>(N), 128,
+                   static_cast<uint32_t>(kc.b_box_rows)) ||
+        !encode_2d(&tc, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, C, static_cast<uint64_t>(N), static_cast<uint64_t>(M),
+                   static_cast<uint32_t>(kc.epi_cols), 32)) {
+        return HGEMM_ERR_CUDA;
+    }
+    GemmParams p{};
+    p.M = M;
+    p.N = N;
+    p.K = K;
+    p.num_m_blocks = (M + kc.bm - 1) / kc.bm;
+    p.num_n_blocks = (N + kc.bn - 1) / kc.bn;
+    p.num_k_blocks = (K + 127) / 128;
+    p.group_m = 16;
+    p.scale_a = sa;
+    p.scale_b = sb;
+    p.dp_tiles = p.num_m_blocks * p.num_n_blocks;
+    p.sfa = static_cast<const uint8_t*>(sfa);
+    p.sfb = static_cast<const uint8_t*>(sfb);
+    p.sf_k_atoms = (K + 127) / 128;
+    const PeerOutputs peers{};
+    const int grid = std::min(p.dp_tiles, dev->num_sms);
+    return kc.launch(ta, tb, tc, p, peers, grid, stream);
+}
+
 }  // namespace
 }  // namespace hg
 
 extern "C" {
+
+int hgemm_fp8_tn_mx(const void* A, const void* B, void* C, int M, int N, int K, const void* SFA, const void* SFB,
+                    const float* d_scale_a, const float* d_scale_b, hgemm_stream_t stream) {
+    return hg::run_gemm_mx(A, B, C, M, N, K, SFA, SFB, d_scale_a, d_scale_b, reinterpret_cast<cudaStream_t>(stream));
+}
+
+size_t hgemm_mx_sf_bytes(int rows, int K) {
+    if (rows <= 0 || K <= 0) return 0;
+    return static_cast<size_t>((rows + 127) / 128) * static_cast<size_t>((K + 127) / 128) * 512;
+}
+
+int hgemm_host_mx_sf_to_blocked(const uint8_t* sf, int rows, int K, uint8_t* blocked) {
+    if (rows < 0 || K < 0 || K % 32 != 0 || (rows > 0 && K > 0 && (!sf || !blocked))) return HGEMM_ERR_INVALID_VALUE;
+    const int groups = K / 32, k_atoms = (K + 127) / 128, row_atoms = (rows + 127) / 128;
+    // Padding (rows past `rows`, groups past K/32) holds 127 = 2^0, a finite scale.
+    std::memset(blocked, 127, hgemm_mx_sf_bytes(rows, K));
+    (void)row_atoms;
+    for (int r = 0; r < rows; ++r) {
+        for (int g = 0; g < groups; ++g) {
+            const size_t atom = static_cast<size_t>(r / 128) * k_atoms + g / 4;
+            const int rr = r % 128;
+            blocked[atom * 512 + 16 * (rr % 32) + 4 * (rr / 32) + (g % 4)] = sf[static_cast<size_t>(r) * groups + g];
+        }
+    }
+    return HGEMM_OK;
+}
+
 
 int hgemm_fp8_tn(const void* A, const void* B, void* C, int M, int N, int K, const float* d_scale_a,
                  const float* d_scale_b, hgemm_stream_t stream) {

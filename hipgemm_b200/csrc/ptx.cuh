@@ -327,6 +327,54 @@ __host__ __device__ constexpr uint32_t idesc_e4m3_f32(int m, int n) {
            (static_cast<uint32_t>(m >> 4) << 24);
 }
 
+// ---- MX block scaling (kind::mxf8f6f4.block_scale) ---------------------------------------
+
+// 1-D bulk copy global -> this CTA's shared memory (16-byte aligned, size % 16 == 0),
+// completing `bar`.
+__device__ __forceinline__ void bulk_load_1d(uint32_t smem_dst, const void* src, uint32_t bytes, uint32_t bar) {
+    asm volatile("cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(
+                     smem_dst),
+                 "l"(reinterpret_cast<uint64_t>(src)), "r"(bytes), "r"(bar)
+                 : "memory");
+}
+
+// Shared -> tensor memory: 32 rows x 128 bits, written to lanes [0, 32) of all four lane
+// quadrants (columns taddr .. taddr + 3).  Issued by one thread; ordered with the
+// thread's later tcgen05.mma.
+__device__ __forceinline__ void tmem_cp_32x128b_warpx4(uint32_t taddr, uint64_t src_desc) {
+    asm volatile("tcgen05.cp.cta_group::1.32x128b.warpx4 [%0], %1;" ::"r"(taddr), "l"(src_desc) : "memory");
+}
+
+// Descriptor of a 32 x 16-byte scale-factor block in shared memory: no swizzle, K-major,
+// rows 16 bytes apart, 8-row core matrices 128 bytes apart (stride byte offset).
+__device__ __forceinline__ uint64_t sf_smem_desc(uint32_t smem_addr) {
+    uint64_t d = 0;
+    d |= static_cast<uint64_t>((smem_addr & 0x3FFFFu) >> 4);
+    d |= static_cast<uint64_t>(128u >> 4) << 32;
+    d |= static_cast<uint64_t>(1u) << 46;  // version 1, swizzle mode 0
+    return d;
+}
+
+// Instruction descriptor for kind::mxf8f6f4 with e4m3 A/B, e8m0 scale factors (one per 32
+// K elements), both operands K-major: B scale-factor byte at [4,6), formats at [7,10) and
+// [10,13) (0 = e4m3), N>>3 at [17,23), scale format e8m0 (1) at bit 23, M>>4 at [24,29),
+// A scale-factor byte at [29,31).  sf_id picks the byte of each 32-bit tensor-memory
+// column that this MMA's K slice uses.
+__host__ __device__ constexpr uint32_t idesc_mx_e4m3(int m, int n, uint32_t sf_id) {
+    return (sf_id << 4) | (static_cast<uint32_t>(n >> 3) << 17) | (1u << 23) | (static_cast<uint32_t>(m >> 4) << 24) |
+           (sf_id << 29);
+}
+
+__device__ __forceinline__ void mma_mxf8f6f4(uint32_t d_tmem, uint64_t a_desc, uint64_t b_desc, uint32_t idesc,
+                                             uint32_t tsfa, uint32_t tsfb, uint32_t accumulate) {
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "setp.ne.b32 p, %4, 0;\n\t"
+        "tcgen05.mma.cta_group::1.kind::mxf8f6f4.block_scale [%0], %1, %2, %3, [%5], [%6], p;\n\t}\n" ::"r"(d_tmem),
+        "l"(a_desc), "l"(b_desc), "r"(idesc), "r"(accumulate), "r"(tsfa), "r"(tsfb)
+        : "memory");
+}
+
 // ---- conversions -------------------------------------------------------------------------
 
 // Two fp32 -> packed bf16x2 with round-to-nearest-even; `lo` lands in the low half.

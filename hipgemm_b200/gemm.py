@@ -185,3 +185,38 @@ def fp8_gemm_tn_from_host(a_host: torch.Tensor, b_host: torch.Tensor, c_host: to
                                           _ptr(d_scales), _stream_handle(stream))
     check(rc, "hgemm_fp8_tn_from_host")
     return c_host
+
+
+def mx_sf_to_blocked(sf: torch.Tensor, K: int) -> torch.Tensor:
+    """Row-major e8m0 scale factors (rows x K/32, uint8, CPU) -> the blocked layout the MX
+    kernel reads (hgemm_host_mx_sf_to_blocked); returns a CPU uint8 tensor."""
+    if sf.is_cuda or sf.dtype != torch.uint8 or sf.dim() != 2 or sf.shape[1] * 32 != K:
+        raise ValueError("sf must be a CPU uint8 (rows, K/32) tensor")
+    sf = sf.contiguous()
+    rows = sf.shape[0]
+    out = torch.empty(int(lib().hgemm_mx_sf_bytes(rows, K)), dtype=torch.uint8)
+    check(lib().hgemm_host_mx_sf_to_blocked(sf.data_ptr(), rows, K, out.data_ptr()), "hgemm_host_mx_sf_to_blocked")
+    return out
+
+
+def fp8_gemm_tn_mx(a: torch.Tensor, b: torch.Tensor, sfa_blocked: torch.Tensor, sfb_blocked: torch.Tensor,
+                   scale_a: torch.Tensor | None = None, scale_b: torch.Tensor | None = None,
+                   out: torch.Tensor | None = None, stream: torch.cuda.Stream | None = None) -> torch.Tensor:
+    """OCP MX e4m3 GEMM (one e8m0 scale per 32 K elements of each row of a and b, blocked
+    layout from mx_sf_to_blocked, on the device): C = sa*sb * sum_k (a 2^sfa)(b 2^sfb)."""
+    _check_operand("a", a)
+    _check_operand("b", b)
+    M, K = a.shape
+    N = b.shape[0]
+    for name, t, rows in (("sfa_blocked", sfa_blocked, M), ("sfb_blocked", sfb_blocked, N)):
+        if not t.is_cuda or t.dtype != torch.uint8 or t.numel() < int(lib().hgemm_mx_sf_bytes(rows, K)):
+            raise ValueError(f"{name} must be a CUDA uint8 tensor of hgemm_mx_sf_bytes({rows}, {K}) bytes")
+    _check_scale("scale_a", scale_a, a.device)
+    _check_scale("scale_b", scale_b, a.device)
+    if out is None:
+        out = torch.empty((M, N), dtype=torch.bfloat16, device=a.device)
+    with torch.cuda.device(a.device):
+        rc = lib().hgemm_fp8_tn_mx(a.data_ptr(), b.data_ptr(), out.data_ptr(), M, N, K, sfa_blocked.data_ptr(),
+                                   sfb_blocked.data_ptr(), _ptr(scale_a), _ptr(scale_b), _stream_handle(stream))
+    check(rc, "hgemm_fp8_tn_mx")
+    return out

@@ -171,6 +171,25 @@ const char* hgemm_error_string(int code);
 /* Library version string. */
 const char* hgemm_version(void);
 
+/* ---- MX block scaling ------------------------------------------------------------------- */
+
+/* OCP MX e4m3 GEMM (tcgen05 kind::mxf8f6f4.block_scale): every 32 consecutive K elements of
+ * a row of A and of B carry their own e8m0 scale (2^(e - 127)), so
+ *   C = bf16_rne((scale_a*scale_b) * sum_k A[m][k] 2^(SFA[m][k/32]-127) B[n][k] 2^(SFB[n][k/32]-127)).
+ * SFA / SFB are in the blocked layout that tcgen05 consumes (hgemm_host_mx_sf_to_blocked
+ * converts from row-major rows x K/32): 512-byte atoms of 128 rows x 4 K-groups, row r,
+ * group g at byte 16*(r%32) + 4*(r/32) + g; atom (r/128, g/4) at ((r/128)*ceil(K/128) +
+ * g/4) * 512; hgemm_mx_sf_bytes() bytes each, 16-byte aligned.  Padding entries must hold
+ * a finite scale (not 0xFF).  K % 32 == 0 and N % 8 == 0.  The reference's MFMA builtin
+ * is the block-scaled instruction with its scales fixed at zero (fp8_4wave.hpp:53-58);
+ * this is that instruction with scales in use. */
+int hgemm_fp8_tn_mx(const void* A, const void* B, void* C, int M, int N, int K, const void* SFA, const void* SFB,
+                    const float* d_scale_a, const float* d_scale_b, hgemm_stream_t stream);
+/* Bytes of a blocked scale-factor tensor for `rows` rows and K columns. */
+size_t hgemm_mx_sf_bytes(int rows, int K);
+/* Row-major (rows x K/32) e8m0 bytes -> the blocked layout above (host memory). */
+int hgemm_host_mx_sf_to_blocked(const uint8_t* sf, int rows, int K, uint8_t* blocked);
+
 /* ---- device quantiser ------------------------------------------------------------------- */
 
 #define HGEMM_DTYPE_F32 0

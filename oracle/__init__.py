@@ -40,6 +40,8 @@ _SIG = {
     "oracle_validate_reference": (_i, [_vp, _vp, _i, _i]),
     "oracle_max_threads": (_i, []),
     "oracle_mt19937_nth": (ctypes.c_uint32, [ctypes.c_uint32, ctypes.c_uint64]),
+    "oracle_quantize_mx_e4m3": (None, [_vp, _i, _i, _vp, _vp]),
+    "oracle_gemm_mx_rows": (None, [_vp, _vp, _vp, _vp, _vp, _i, _i, _f, _f, _i, _i, _i]),
 }
 
 RTOL = 1e-2  # benchmark-config tolerance: |c - ref| <= RTOL*|ref| + ATOL per element
@@ -183,3 +185,24 @@ def max_threads() -> int:
 def mt19937_nth(seed: int, n: int) -> int:
     """The n-th (1-based) output of std::mt19937(seed)."""
     return int(lib().oracle_mt19937_nth(seed, n))
+
+
+def quantize_mx(x: np.ndarray) -> tuple[np.ndarray, np.ndarray]:
+    """OCP MX e4m3: (q rows x K, e8m0 scales rows x K/32) of a rows x K fp32 array."""
+    x = np.ascontiguousarray(x, dtype=np.float32)
+    rows, K = x.shape
+    q = np.empty((rows, K), dtype=np.uint8)
+    sf = np.empty((rows, K // 32), dtype=np.uint8)
+    lib().oracle_quantize_mx_e4m3(_p(x), rows, K, _p(q), _p(sf))
+    return q, sf
+
+
+def gemm_mx(A, B, SFA, SFB, scale_a=1.0, scale_b=1.0, row_begin=0, row_end=None, nthreads=0) -> np.ndarray:
+    """bf16 bits of rows [row_begin, row_end) of the block-scaled product."""
+    M, K = A.shape
+    N = B.shape[0]
+    row_end = M if row_end is None else row_end
+    C = np.empty((row_end - row_begin, N), dtype=np.uint16)
+    lib().oracle_gemm_mx_rows(_p(A), _p(B), _p(np.ascontiguousarray(SFA)), _p(np.ascontiguousarray(SFB)), _p(C), N, K,
+                              scale_a, scale_b, row_begin, row_end, nthreads)
+    return C

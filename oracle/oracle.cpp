@@ -265,4 +265,73 @@ int oracle_validate_reference(const uint16_t* C, const uint16_t* C_ref, int M, i
 
 int oracle_max_threads(void) { return resolve_threads(0); }
 
+// ---- MX block scaling ---------------------------------------------------------------------
+
+// OCP Microscaling Formats (MX) v1.0, e4m3 elements, e8m0 shared scale per 32 elements of a
+// row: X = floor(log2(max |x|)) - 8 (8 is e4m3's largest exponent), clamped to [-127, 127],
+// with X = -127 for an all-zero block; scale byte = X + 127; element = e4m3(x * 2^-X),
+// round-to-nearest-even, saturating to +-448.
+void oracle_quantize_mx_e4m3(const float* x, int rows, int K, uint8_t* q, uint8_t* sf) {
+    const int groups = K / 32;
+    for (int r = 0; r < rows; ++r) {
+        for (int g = 0; g < groups; ++g) {
+            const float* v = x + size_t(r) * K + size_t(g) * 32;
+            float amax = 0.0f;
+            for (int i = 0; i < 32; ++i) amax = std::max(amax, std::fabs(v[i]));
+            int X = -127;
+            if (amax > 0.0f && std::isfinite(amax)) {
+                int e;
+                std::frexp(amax, &e);  // amax = f * 2^e, f in [0.5, 1): floor(log2(amax)) = e - 1
+                X = std::min(127, std::max(-127, (e - 1) - 8));
+            }
+            sf[size_t(r) * groups + g] = uint8_t(X + 127);
+            for (int i = 0; i < 32; ++i) q[size_t(r) * K + size_t(g) * 32 + i] = encode_e4m3(std::ldexp(v[i], -X));
+        }
+    }
+}
+
+// The block-scaled product in the reference's loop order (test.cpp:19-30): per element one
+// fp32 accumulator, k ascending, each term A*2^(ea-127) * B*2^(eb-127) (exact in fp32 for
+// scales inside its range), then bf16_rne((scale_a*scale_b) * acc).  SFA / SFB row-major,
+// K/32 bytes per row; a scale byte of 255 is NaN.
+void oracle_gemm_mx_rows(const uint8_t* A, const uint8_t* B, const uint8_t* SFA, const uint8_t* SFB, uint16_t* C_rows,
+                         int N, int K, float scale_a, float scale_b, int row_begin, int row_end, int nthreads) {
+    const int groups = K / 32;
+    const float s = scale_a * scale_b;
+    const int nt = resolve_threads(nthreads);
+    (void)nt;
+    auto scaled = [](uint8_t v, uint8_t e) {
+        return e == 255 ? NAN : std::ldexp(kDecode.v[v], int(e) - 127);
+    };
+#pragma omp parallel num_threads(nt)
+    {
+        std::vector<float> bt, arow(K);
+#pragma omp for schedule(dynamic, 1)
+        for (int cb = 0; cb < (N + kColBlock - 1) / kColBlock; ++cb) {
+            const int col0 = cb * kColBlock, nc = std::min(kColBlock, N - col0);
+            bt.assign(size_t(K) * kColBlock, 0.0f);
+            for (int j = 0; j < nc; ++j) {
+                const uint8_t* b = B + size_t(col0 + j) * K;
+                const uint8_t* eb = SFB + size_t(col0 + j) * groups;
+                for (int k = 0; k < K; ++k) bt[size_t(k) * kColBlock + j] = scaled(b[k], eb[k / 32]);
+            }
+            for (int r = row_begin; r < row_end; ++r) {
+                const uint8_t* a = A + size_t(r) * K;
+                const uint8_t* ea = SFA + size_t(r) * groups;
+                for (int k = 0; k < K; ++k) arow[k] = scaled(a[k], ea[k / 32]);
+                float acc[kColBlock];
+                for (int j = 0; j < kColBlock; ++j) acc[j] = 0.0f;
+                for (int k = 0; k < K; ++k) {
+                    const float av = arow[k];
+                    const float* bk = bt.data() + size_t(k) * kColBlock;
+#pragma GCC ivdep
+                    for (int j = 0; j < kColBlock; ++j) acc[j] += av * bk[j];
+                }
+                uint16_t* c = C_rows + size_t(r - row_begin) * N + col0;
+                for (int j = 0; j < nc; ++j) c[j] = bf16_rne(s * acc[j]);
+            }
+        }
+    }
+}
+
 }  // extern "C"

@@ -95,6 +95,15 @@ int64_t oracle_validate(const uint16_t* C, const uint16_t* C_ref, int64_t n, flo
  * `diff > c_ref*0.01`, stops at the first mismatch.  Returns 1 when it passes. */
 int oracle_validate_reference(const uint16_t* C, const uint16_t* C_ref, int M, int N);
 
+/* OCP MX v1.0 e4m3 quantisation with an e8m0 scale per 32 elements of a row: X =
+ * floor(log2(amax)) - 8 clamped to [-127, 127] (-127 for a zero block), scale byte X + 127,
+ * q = e4m3(x * 2^-X).  x and q: rows x K (K % 32 == 0); sf: rows x K/32. */
+void oracle_quantize_mx_e4m3(const float* x, int rows, int K, uint8_t* q, uint8_t* sf);
+/* Block-scaled GEMM rows [row_begin, row_end) into C_rows, sequential fp32 accumulation of
+ * A*2^(ea-127) * B*2^(eb-127), then bf16_rne((scale_a*scale_b) * acc); SFA, SFB row-major. */
+void oracle_gemm_mx_rows(const uint8_t* A, const uint8_t* B, const uint8_t* SFA, const uint8_t* SFB, uint16_t* C_rows,
+                         int N, int K, float scale_a, float scale_b, int row_begin, int row_end, int nthreads);
+
 /* Threads OpenMP would use. */
 int oracle_max_threads(void);
 

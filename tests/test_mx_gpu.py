@@ -1,0 +1,94 @@
+"""The MX block-scaled GEMM (tcgen05 kind::mxf8f6f4.block_scale) against the oracle's
+block-scaled product: OCP MX e4m3 inputs with one e8m0 scale per 32 K elements, scales
+spread over many binades, ragged shapes.
+
+Tolerance: |c - ref| <= 1e-2*|ref| + 1e-3 + 2^-16 * sum_k |a_k b_k| (all after the per-tensor
+scales).  The first two terms are the per-tensor tests' bound.  The third allows for fp32
+summation in a different order: with scales 2^-8 .. 2^8 per block an element can cancel
+millions of times over (sum |a b| / |sum a b| ~ 1e6 occurs at 300x520x1056), and then any two
+fp32 orders differ by ulps of sum |a b|, the oracle's sequential order included.  2^-16 is
+about four times the random-walk error sqrt(K) * 2^-24 at K = 4096; for a well-conditioned
+element it adds less than 1e-3 relative."""
+import numpy as np
+import pytest
+import torch
+
+import oracle
+from tests.gemm_cases import c_bits, sample_rows
+
+pytestmark = pytest.mark.gpu
+
+
+def _abs_products(A, B, SFA, SFB, rows, scale):
+    """sum_k |a_k b_k| (float64) for the given rows of A against every row of B."""
+    T = np.abs(oracle.decode_table().astype(np.float64))
+    a = T[A[rows]] * np.ldexp(1.0, SFA[rows].astype(np.int64) - 127).repeat(32, axis=1)
+    b = T[B] * np.ldexp(1.0, SFB.astype(np.int64) - 127).repeat(32, axis=1)
+    return (a @ b.T) * abs(scale)
+
+
+def _mismatches(got, ref, absum):
+    g = oracle.bf16_to_f32(got).astype(np.float64)
+    r = oracle.bf16_to_f32(ref).astype(np.float64)
+    bad = ~(np.abs(g - r) <= 1e-2 * np.abs(r) + 1e-3 + 2.0 ** -16 * absum)
+    idx = np.flatnonzero(bad)
+    return int(idx.size), (int(idx[0]), g.flat[idx[0]], r.flat[idx[0]]) if idx.size else None
+
+
+def _mx_operand(rows, K, seed):
+    rng = np.random.default_rng(seed)
+    # Magnitudes spread over 2^-8 .. 2^8 per row and per 32-block, so scales differ.
+    mag = np.ldexp(1.0, rng.integers(-8, 9, (rows, K // 32))).repeat(32, axis=1)
+    x = (oracle.normal_f32(rows * K, seed).reshape(rows, K) * mag).astype(np.float32)
+    return oracle.quantize_mx(x)
+
+
+@pytest.mark.parametrize("M,N,K", [(128, 128, 128), (256, 384, 1024), (300, 520, 1056), (1000, 1032, 2080),
+                                   (4096, 4096, 4096)])
+def test_mx_gemm_matches_oracle(cuda_device, M, N, K):
+    import hipgemm_b200 as hg
+    A, SFA = _mx_operand(M, K, M)
+    B, SFB = _mx_operand(N, K, N + 1)
+    sfa = hg.mx_sf_to_blocked(torch.from_numpy(SFA), K).cuda()
+    sfb = hg.mx_sf_to_blocked(torch.from_numpy(SFB), K).cuda()
+    sa = torch.tensor([0.75], dtype=torch.float32, device="cuda")
+    sb = torch.tensor([1.5], dtype=torch.float32, device="cuda")
+    c = hg.fp8_gemm_tn_mx(torch.from_numpy(A).cuda(), torch.from_numpy(B).cuda(), sfa, sfb, sa, sb)
+    torch.cuda.synchronize()
+    assert hg.device_status() == 0
+    got = c_bits(c)
+    rows = np.arange(M) if M * N * K <= 2**31 else sample_rows(M, 64)
+    if rows.size == M:
+        ref = oracle.gemm_mx(A, B, SFA, SFB, 0.75, 1.5)
+    else:
+        ref = np.concatenate([oracle.gemm_mx(A, B, SFA, SFB, 0.75, 1.5, r, r + 1) for r in rows])
+    bad, first = _mismatches(np.ascontiguousarray(got[rows]), ref, _abs_products(A, B, SFA, SFB, rows, 0.75 * 1.5))
+    assert bad == 0, f"{bad} mismatches (first: flat index, got, ref = {first})"
+    # The standard tolerance alone must hold almost everywhere: only badly cancelling
+    # elements may need the third term.
+    assert oracle.validate(np.ascontiguousarray(got[rows]), ref)[0] <= max(1, ref.size // 10000)
+
+
+def test_mx_unit_scales_equal_plain_gemm(cuda_device):
+    """All scale bytes 127 (2^0): the MX kernel must give the plain e4m3 GEMM's bits."""
+    import hipgemm_b200 as hg
+    M, N, K = 512, 640, 1024
+    A, _ = oracle.make_quantized((M, K), 3)
+    B, _ = oracle.make_quantized((N, K), 4)
+    ones_a = hg.mx_sf_to_blocked(torch.full((M, K // 32), 127, dtype=torch.uint8), K).cuda()
+    ones_b = hg.mx_sf_to_blocked(torch.full((N, K // 32), 127, dtype=torch.uint8), K).cuda()
+    a, b = torch.from_numpy(A).cuda(), torch.from_numpy(B).cuda()
+    mx = hg.fp8_gemm_tn_mx(a, b, ones_a, ones_b)
+    plain = hg.fp8_gemm_tn(a, b)
+    ref = oracle.gemm(A, B)
+    assert oracle.validate(c_bits(mx), ref)[0] == 0
+    assert oracle.validate(c_bits(plain), ref)[0] == 0
+
+
+def test_mx_argument_checks(cuda_device):
+    import hipgemm_b200 as hg
+    a = torch.zeros((64, 48), dtype=torch.uint8, device="cuda")
+    sf = torch.zeros(4096, dtype=torch.uint8, device="cuda")
+    with pytest.raises(hg.HgemmError) as e:
+        hg.fp8_gemm_tn_mx(a, a, sf, sf)  # K % 32 != 0
+    assert e.value.code == hg.HGEMM_ERR_ALIGNMENT

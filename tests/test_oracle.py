@@ -198,3 +198,60 @@ def test_reference_validator_signed_threshold_bug():
     assert oracle.validate(C, C)[0] == 0
     P = oracle.bf16_rne_array(np.array([[1.0, 2.0]], dtype=np.float32))
     assert oracle.validate_reference(P, P)
+
+
+# ---- MX block scaling ------------------------------------------------------------------------
+
+def test_mx_quantiser_known_answers():
+    x = np.zeros((2, 96), dtype=np.float32)
+    x[0, :32] = np.linspace(-448, 448, 32)       # amax 448 = 1.75 * 2^8: X = 0, scale byte 127
+    x[0, 32:64] = np.linspace(-1, 1, 32)         # amax 1: X = -8, elements scaled by 2^8
+    x[0, 64:96] = 3e-3                            # amax 3e-3 in [2^-9, 2^-8): X = -9 - 8 = -17
+    q, sf = oracle.quantize_mx(x)
+    assert sf.tolist() == [[127, 119, 110], [0, 0, 0]]  # an all-zero block gets X = -127
+    assert q[0, 63] == oracle.fp8_encode(256.0) == 0x78
+    assert q[0, 0] == 0xFE and q[0, 31] == 0x7E
+    assert int(np.count_nonzero(q[1])) == 0
+    assert q[0, 64] == oracle.fp8_encode(np.float32(3e-3) * np.float32(2.0 ** 17))
+
+
+def _numpy_mx(A, B, SFA, SFB, sa, sb):
+    T = oracle.decode_table().astype(np.float64)
+    sa_ = np.ldexp(1.0, SFA.astype(np.int64) - 127).repeat(32, axis=1)
+    sb_ = np.ldexp(1.0, SFB.astype(np.int64) - 127).repeat(32, axis=1)
+    a = (T[A] * sa_).astype(np.float32)
+    b = (T[B] * sb_).astype(np.float32)
+    acc = np.zeros((A.shape[0], B.shape[0]), dtype=np.float32)
+    for k in range(A.shape[1]):
+        acc += np.outer(a[:, k], b[:, k]).astype(np.float32)
+    s = np.float32(np.float32(sa) * np.float32(sb))
+    return oracle.bf16_rne_array((s * acc).astype(np.float32))
+
+
+@pytest.mark.parametrize("M,N,K", [(3, 5, 32), (17, 24, 128), (40, 33, 320)])
+def test_mx_gemm_matches_numpy_restatement(M, N, K):
+    rng = np.random.default_rng(M)
+    xa = (rng.standard_normal((M, K)) * np.ldexp(1.0, rng.integers(-6, 6, (M, 1)))).astype(np.float32)
+    xb = (rng.standard_normal((N, K)) * np.ldexp(1.0, rng.integers(-6, 6, (N, 1)))).astype(np.float32)
+    A, SFA = oracle.quantize_mx(xa)
+    B, SFB = oracle.quantize_mx(xb)
+    assert np.array_equal(oracle.gemm_mx(A, B, SFA, SFB, 0.5, 2.0), _numpy_mx(A, B, SFA, SFB, 0.5, 2.0))
+
+
+@pytest.mark.parametrize("rows,K", [(1, 32), (128, 128), (130, 96), (300, 1056)])
+def test_mx_blocked_scale_layout(rows, K):
+    """The product's host converter against the layout written out here: 512-byte atoms of
+    128 rows x 4 groups, row r group g at 16*(r%32) + 4*(r/32) + g, atoms K-major."""
+    import torch
+    import hipgemm_b200 as hg
+    rng = np.random.default_rng(rows + K)
+    sf = rng.integers(0, 255, (rows, K // 32), dtype=np.uint8)
+    got = hg.mx_sf_to_blocked(torch.from_numpy(sf), K).numpy()
+    k_atoms = (K + 127) // 128
+    want = np.full(((rows + 127) // 128) * k_atoms * 512, 127, dtype=np.uint8)
+    for r in range(rows):
+        for g in range(K // 32):
+            atom = (r // 128) * k_atoms + g // 4
+            rr = r % 128
+            want[atom * 512 + 16 * (rr % 32) + 4 * (rr // 32) + g % 4] = sf[r, g]
+    assert np.array_equal(got, want)

@@ -204,6 +204,14 @@ __device__ __forceinline__ void st_global_v4(float* p, float a, float b, float c
     asm volatile("st.global.v4.f32 [%0], {%1, %2, %3, %4};" ::"l"(p), "f"(a), "f"(b), "f"(c), "f"(d) : "memory");
 }
 
+// Scale-factor atoms (128 rows of B each) that column block nb of width 128 * ATOMS covers
+// inside N: ATOMS except for a last block that ends within the tile.
+template <int ATOMS>
+__device__ __forceinline__ int sfb_atoms_in_tile(const GemmParams& p, int nb) {
+    const int left = (p.N + 127) / 128 - nb * ATOMS;
+    return left < ATOMS ? left : ATOMS;
+}
+
 template <int CTAS, int BN, int STAGES, bool MX = false>
 struct KernelShape {
     static constexpr int BM = 128 * CTAS;   // output tile rows
@@ -214,10 +222,16 @@ struct KernelShape {
     static constexpr int A_BYTES = 128 * BK;
     static constexpr int B_BYTES = B_ROWS * BK;
     static constexpr int STAGE_BYTES = A_BYTES + B_BYTES;
+    // MX with BN > 128: the scale factors need tensor-memory columns that a second
+    // accumulator would take, so there is one accumulator, and the epilogue frees it as soon
+    // as the tile sits in registers (bf16), before its stores.
+    static constexpr int ACC_BUFS = (MX && BN > 128) ? 1 : 2;
+    static constexpr bool EARLY_RELEASE = ACC_BUFS == 1;
     // bf16 columns per staged epilogue chunk: 64 (128-byte rows, 128-byte swizzle) when
-    // BN allows, else 32 (64-byte rows, 64-byte swizzle).
-    static constexpr int EPI_COLS = BN % 64 == 0 ? 64 : 32;
-    static constexpr int EPI_BUF_BYTES = 32 * 64 * 2;  // one warp's 32 rows x 128 B (either width fits)
+    // BN allows, else 32 (64-byte rows, 64-byte swizzle; also the one-accumulator MX tile,
+    // to fit four stages).
+    static constexpr int EPI_COLS = (BN % 64 == 0 && !EARLY_RELEASE) ? 64 : 32;
+    static constexpr int EPI_BUF_BYTES = 32 * EPI_COLS * 2;  // one warp's 32 rows
     static constexpr int OFF_A = 0;
     static constexpr int OFF_B = OFF_A + STAGES * A_BYTES;
     static constexpr int OFF_EPI = OFF_B + STAGES * B_BYTES;
@@ -229,16 +243,18 @@ struct KernelShape {
     static constexpr int NUM_BARS = 2 * STAGES + 5;  // full, empty, tfull x2, tempty x2, drain
     static constexpr int OFF_MISC = OFF_BAR + NUM_BARS * 8;
     static constexpr int SMEM_BYTES = OFF_MISC + 16 + 1024;  // + slack to align the base to 1024 B
-    // Two accumulators of BN fp32 columns, plus (MX) per-stage scale-factor columns (4 per
-    // 128 rows of A and of B), rounded up to the power of two tcgen05.alloc takes.
+    // ACC_BUFS accumulators of BN fp32 columns, plus (MX) per-stage scale-factor columns (4
+    // per 128 rows of A and of B), rounded up to the power of two tcgen05.alloc takes.
     static constexpr int SF_COLS = MX ? 4 * (1 + SFB_ATOMS) : 0;
-    static constexpr int COLS_USED = 2 * BN + STAGES * SF_COLS;
+    static constexpr int OFF_SF_COL = ACC_BUFS * BN;
+    static constexpr int COLS_USED = ACC_BUFS * BN + STAGES * SF_COLS;
     static constexpr uint32_t TMEM_COLS =
         COLS_USED <= 32 ? 32 : (COLS_USED <= 64 ? 64 : (COLS_USED <= 128 ? 128 : (COLS_USED <= 256 ? 256 : 512)));
     static constexpr uint32_t IDESC = idesc_e4m3_f32(BM, BN);
     static constexpr int PARTIAL_FLOATS = 128 * BN;  // one CTA's share of a partial tile
     static_assert(CTAS == 1 || CTAS == 2, "one CTA or a CTA pair");
     static_assert(!MX || CTAS == 1, "MX block scaling is built for the single-CTA tile");
+    static_assert(!MX || BN % 128 == 0, "MX tiles cover whole 128-row scale-factor atoms of B");
     static_assert(COLS_USED <= 512, "tensor memory holds 512 columns");
     static_assert(BN % 32 == 0 && BN >= 64 && BN <= 256, "BN must be a multiple of 32 in [64, 256]");
     static_assert(CTAS == 1 || BN % 16 == 0, "M=256 MMAs need N % 16 == 0");
@@ -335,7 +351,10 @@ __global__ void __launch_bounds__(192, 1)
                         // For a pair: the MMAs that read this stage finished in both CTAs.
                         if (kPair && !first_pass) mbar_arrive_cluster(peer_empty0 + 8 * stage);
                         const uint32_t full = bar_full + 8 * stage;
-                        mbar_arrive_expect_tx(full, CTAS * S::STAGE_BYTES + S::SF_BYTES);
+                        // MX: B's 128-row scale-factor atoms of this tile that exist (a tile
+                        // wider than the rest of N has fewer; its columns past N are clipped).
+                        const int sfb_atoms = MX ? sfb_atoms_in_tile<S::SFB_ATOMS>(p, nb) : 0;
+                        mbar_arrive_expect_tx(full, CTAS * S::STAGE_BYTES + (MX ? 512 * (1 + sfb_atoms) : 0));
                         tma_load_2d(a_dst, &tm_a, kb * S::BK, a_row, full);
                         tma_load_2d(b_dst, &tm_b, kb * S::BK, b_row, full);
                         if constexpr (MX) {
@@ -346,6 +365,7 @@ __global__ void __launch_bounds__(192, 1)
                             bulk_load_1d(sf_dst, p.sfa + (static_cast<size_t>(mb) * ka + kb) * 512, 512, full);
 #pragma unroll
                             for (int i = 0; i < S::SFB_ATOMS; ++i) {
+                                if (i >= sfb_atoms) break;
                                 const size_t rb = static_cast<size_t>(nb) * S::SFB_ATOMS + i;
                                 bulk_load_1d(sf_dst + 512 * (1 + i), p.sfb + (rb * ka + kb) * 512, 512, full);
                             }
@@ -381,6 +401,8 @@ __global__ void __launch_bounds__(192, 1)
                 }
                 tc_fence_after();
                 const uint32_t d_tmem = tmem_base + static_cast<uint32_t>(acc * BN);
+                int mma_mb = 0, mma_nb = 0;
+                if constexpr (MX) tile_coords(w.tile, p, mma_mb, mma_nb);
                 for (int kb = w.kb_begin; kb < w.kb_end; ++kb) {
                     if (!mbar_wait<kPair>(bar_full + 8 * stage, phase, abort_flag, kErrMmaFull)) {
                         ok = false;
@@ -392,12 +414,14 @@ __global__ void __launch_bounds__(192, 1)
                     if constexpr (MX) {
                         // Scale factors of this stage into its tensor-memory columns: A's at
                         // tsfa (4 columns), B's after them; the MMAs below read them in order.
-                        const uint32_t tsfa = tmem_base + static_cast<uint32_t>(2 * BN + stage * S::SF_COLS);
+                        const uint32_t tsfa = tmem_base + static_cast<uint32_t>(S::OFF_SF_COL + stage * S::SF_COLS);
                         const uint32_t tsfb = tsfa + 4;
                         const uint32_t sf_src = base + S::OFF_SF + stage * S::SF_BYTES;
                         tmem_cp_32x128b_warpx4(tsfa, sf_smem_desc(sf_src));
+                        const int sfb_atoms = sfb_atoms_in_tile<S::SFB_ATOMS>(p, mma_nb);
 #pragma unroll
                         for (int i = 0; i < S::SFB_ATOMS; ++i) {
+                            if (i >= sfb_atoms) break;
                             tmem_cp_32x128b_warpx4(tsfb + 4 * i, sf_smem_desc(sf_src + 512 * (1 + i)));
                         }
 #pragma unroll
@@ -427,7 +451,7 @@ __global__ void __launch_bounds__(192, 1)
                 }
                 if (!ok) break;
                 mma_commit<CTAS>(bar_tfull + 8 * acc);  // accumulator ready for the epilogue
-                if (++acc == 2) {
+                if (++acc == S::ACC_BUFS) {
                     acc = 0;
                     acc_phase ^= 1u;
                 }
@@ -456,14 +480,9 @@ __global__ void __launch_bounds__(192, 1)
 
         constexpr int EC = S::EPI_COLS;
 
-        // Scale EC fp32 accumulators of this thread's row, round to bf16 (RNE), stage them
-        // in this warp's double-buffered 32 x EC tile and TMA-store it at (row0, col0).
-        auto store_chunk = [&](const float (&v)[EC], int row0, int col0) {
-            uint32_t packed[EC / 2];
-#pragma unroll
-            for (int j = 0; j < EC / 2; ++j) {
-                packed[j] = pack_bf16x2_rn(__fmul_rn(v[2 * j], s), __fmul_rn(v[2 * j + 1], s));
-            }
+        // Stage EC bf16 values (packed pairs) of this thread's row in this warp's
+        // double-buffered 32 x EC tile and TMA-store it at (row0, col0).
+        auto store_packed = [&](const uint32_t* packed, int row0, int col0) {
             const uint32_t buf = chunk_ctr & 1u;
             // The store issued two chunks ago read this buffer; wait until it has.
             if (lane == 0) bulk_wait_group_read<1>();
@@ -492,6 +511,16 @@ __global__ void __launch_bounds__(192, 1)
             ++chunk_ctr;
         };
 
+        // Scale EC fp32 accumulators of this thread's row, round to bf16 (RNE) and store.
+        auto store_chunk = [&](const float (&v)[EC], int row0, int col0) {
+            uint32_t packed[EC / 2];
+#pragma unroll
+            for (int j = 0; j < EC / 2; ++j) {
+                packed[j] = pack_bf16x2_rn(__fmul_rn(v[2 * j], s), __fmul_rn(v[2 * j + 1], s));
+            }
+            store_packed(packed, row0, col0);
+        };
+
         auto release_accumulator = [&]() {
             // All lanes' tensor-memory reads are complete (tcgen05.wait::ld).
             tc_fence_before();
@@ -503,7 +532,7 @@ __global__ void __launch_bounds__(192, 1)
                     mbar_arrive_cluster(leader_tempty0 + 8 * acc);
                 }
             }
-            if (++acc == 2) {
+            if (++acc == S::ACC_BUFS) {
                 acc = 0;
                 acc_phase ^= 1u;
             }
@@ -525,6 +554,26 @@ __global__ void __launch_bounds__(192, 1)
             const int row0 = mb * S::BM + static_cast<int>(rank) * 128 + static_cast<int>(quad) * 32;
             const uint32_t tmem_row = tmem_base + ((quad * 32u) << 16) + static_cast<uint32_t>(acc * BN);
 
+            if constexpr (S::EARLY_RELEASE) {
+                // The whole row into registers as bf16, then the accumulator is free for the
+                // next tile's MMAs while this one is stored (data-parallel tiles only).
+                uint32_t packed[BN / 2];
+#pragma unroll
+                for (int c = 0; c < BN / 16; ++c) {
+                    uint32_t r[16];
+                    tmem_ld_32x32b_x16(tmem_row + c * 16, r);
+                    tmem_ld_wait(r);
+#pragma unroll
+                    for (int j = 0; j < 8; ++j) {
+                        packed[8 * c + j] = pack_bf16x2_rn(__fmul_rn(__uint_as_float(r[2 * j]), s),
+                                                           __fmul_rn(__uint_as_float(r[2 * j + 1]), s));
+                    }
+                }
+                release_accumulator();
+#pragma unroll
+                for (int c = 0; c < BN / EC; ++c) store_packed(&packed[c * (EC / 2)], row0, nb * BN + c * EC);
+                continue;
+            }
             if (w.piece < 0) {
 #pragma unroll 1
                 for (int c = 0; c < BN / EC; ++c) {

@@ -104,8 +104,33 @@ const KernelConfig kConfigs[] = {
 };
 constexpr int kNumConfigs = sizeof(kConfigs) / sizeof(kConfigs[0]);
 
-// MX block-scaled kernel: 128 x 128 tiles, 5 stages (the scale-factor atoms take the sixth).
-const KernelConfig kMxConfig = make_config<1, 128, 5, true>("mx_bn128_s5", 1.0);
+// MX block-scaled kernels (index 1 and 2 of hgemm_fp8_tn_mx_config; 0 = choose).
+// 128 x 256 tiles with one accumulator (early release), and 128 x 128 tiles with two for
+// grids too small to fill the GPU with the wide tile.  eff: measured throughput at 8192^3
+// relative to the dense peak of the plain kernel's best config.
+const KernelConfig kMxConfigs[] = {
+    make_config<1, 256, 4, true>("mx_bn256_s4", 0.90),
+    make_config<1, 128, 5, true>("mx_bn128_s5", 0.52),
+};
+constexpr int kNumMxConfigs = sizeof(kMxConfigs) / sizeof(kMxConfigs[0]);
+
+// Fewest estimated tile-time units: waves of tiles over the SMs times the tile's MMA work
+// (BN / 128) over its efficiency.
+int choose_mx_config(int M, int N, int num_sms) {
+    int best = 0;
+    double best_cost = 0.0;
+    for (int c = 0; c < kNumMxConfigs; ++c) {
+        const KernelConfig& k = kMxConfigs[c];
+        const long long tiles = static_cast<long long>((M + k.bm - 1) / k.bm) * ((N + k.bn - 1) / k.bn);
+        const long long waves = (tiles + num_sms - 1) / num_sms;
+        const double cost = static_cast<double>(waves) * (k.bn / 128.0) / k.eff;
+        if (c == 0 || cost < best_cost) {
+            best = c;
+            best_cost = cost;
+        }
+    }
+    return best;
+}
 
 void init_encode() {
     void* fn = nullptr;
@@ -164,10 +189,12 @@ int device_setup(int dev) {
             }
             st.resident_ctas[c] = clusters * k.ctas;
         }
-        if (cudaFuncSetAttribute(kMxConfig.kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                 kMxConfig.smem_bytes) != cudaSuccess) {
-            st.status = HGEMM_ERR_CUDA;
-            return;
+        for (const KernelConfig& k : kMxConfigs) {
+            if (cudaFuncSetAttribute(k.kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, k.smem_bytes) !=
+                cudaSuccess) {
+                st.status = HGEMM_ERR_CUDA;
+                return;
+            }
         }
         // Library-owned stream-ordered pool for stream-K workspaces; it keeps its memory
         // (release threshold = max) so repeated calls do not map pages again.
@@ -387,7 +414,8 @@ int run_gemm(const void* A, const void* B, void* C, int M, int N, int K, const f
 }
 
 int run_gemm_mx(const void* A, const void* B, void* C, int M, int N, int K, const void* sfa, const void* sfb,
-                const float* sa, const float* sb, cudaStream_t stream) {
+                const float* sa, const float* sb, int config, cudaStream_t stream) {
+    if (config < 0 || config > kNumMxConfigs) return HGEMM_ERR_INVALID_VALUE;
     int rc = check_args(A, B, C, M, N, K, 0, HGEMM_SCHEDULE_DATA_PARALLEL);
     if (rc != HGEMM_OK || M == 0 || N == 0) return rc;
     if (K % 32 != 0) return HGEMM_ERR_ALIGNMENT;
@@ -399,14 +427,15 @@ int run_gemm_mx(const void* A, const void* B, void* C, int M, int N, int K, cons
         return cudaMemsetAsync(C, 0, static_cast<size_t>(M) * N * 2, stream) == cudaSuccess ? HGEMM_OK
                                                                                               : HGEMM_ERR_CUDA;
     }
-    const KernelConfig& kc = kMxConfig;
+    const KernelConfig& kc = kMxConfigs[config > 0 ? config - 1 : choose_mx_config(M, N, dev->num_sms)];
     CUtensorMap ta, tb, tc;
     if (!encode_2d(&ta, CU_TENSOR_MAP_DATA_TYPE_UINT8, 1, A, static_cast<uint64_t>(K), static_cast<uint64_t>(M), 128,
                    128) ||
         !encode_2d(&tb, CU_TENSOR_MAP_DATA_TYPE_UINT8, 1, B, static_cast<uint64_t>(K), static_cast<uint64_t>(N), 128,
                    static_cast<uint32_t>(kc.b_box_rows)) ||
         !encode_2d(&tc, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, C, static_cast<uint64_t>(N), static_cast<uint64_t>(M),
-                   static_cast<uint32_t>(kc.epi_cols), 32)) {
+                   static_cast<uint32_t>(kc.epi_cols), 32,
+                   kc.epi_cols == 64 ? CU_TENSOR_MAP_SWIZZLE_128B : CU_TENSOR_MAP_SWIZZLE_64B)) {
         return HGEMM_ERR_CUDA;
     }
     GemmParams p{};
@@ -435,7 +464,22 @@ extern "C" {
 
 int hgemm_fp8_tn_mx(const void* A, const void* B, void* C, int M, int N, int K, const void* SFA, const void* SFB,
                     const float* d_scale_a, const float* d_scale_b, hgemm_stream_t stream) {
-    return hg::run_gemm_mx(A, B, C, M, N, K, SFA, SFB, d_scale_a, d_scale_b, reinterpret_cast<cudaStream_t>(stream));
+    return hg::run_gemm_mx(A, B, C, M, N, K, SFA, SFB, d_scale_a, d_scale_b, 0, reinterpret_cast<cudaStream_t>(stream));
+}
+
+int hgemm_fp8_tn_mx_config(const void* A, const void* B, void* C, int M, int N, int K, const void* SFA,
+                           const void* SFB, const float* d_scale_a, const float* d_scale_b, int config,
+                           hgemm_stream_t stream) {
+    return hg::run_gemm_mx(A, B, C, M, N, K, SFA, SFB, d_scale_a, d_scale_b, config,
+                           reinterpret_cast<cudaStream_t>(stream));
+}
+
+int hgemm_mx_num_configs(void) { return hg::kNumMxConfigs + 1; }
+
+const char* hgemm_mx_config_name(int config) {
+    if (config == 0) return "auto";
+    if (config < 0 || config > hg::kNumMxConfigs) return nullptr;
+    return hg::kMxConfigs[config - 1].name;
 }
 
 size_t hgemm_mx_sf_bytes(int rows, int K) {

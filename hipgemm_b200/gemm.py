@@ -201,9 +201,11 @@ def mx_sf_to_blocked(sf: torch.Tensor, K: int) -> torch.Tensor:
 
 def fp8_gemm_tn_mx(a: torch.Tensor, b: torch.Tensor, sfa_blocked: torch.Tensor, sfb_blocked: torch.Tensor,
                    scale_a: torch.Tensor | None = None, scale_b: torch.Tensor | None = None,
-                   out: torch.Tensor | None = None, stream: torch.cuda.Stream | None = None) -> torch.Tensor:
+                   out: torch.Tensor | None = None, stream: torch.cuda.Stream | None = None,
+                   config: int = 0) -> torch.Tensor:
     """OCP MX e4m3 GEMM (one e8m0 scale per 32 K elements of each row of a and b, blocked
-    layout from mx_sf_to_blocked, on the device): C = sa*sb * sum_k (a 2^sfa)(b 2^sfb)."""
+    layout from mx_sf_to_blocked, on the device): C = sa*sb * sum_k (a 2^sfa)(b 2^sfb).
+    config: 0 chooses by wave count, 1 = 128 x 256 tiles, 2 = 128 x 128 tiles."""
     _check_operand("a", a)
     _check_operand("b", b)
     M, K = a.shape
@@ -216,7 +218,8 @@ def fp8_gemm_tn_mx(a: torch.Tensor, b: torch.Tensor, sfa_blocked: torch.Tensor, 
     if out is None:
         out = torch.empty((M, N), dtype=torch.bfloat16, device=a.device)
     with torch.cuda.device(a.device):
-        rc = lib().hgemm_fp8_tn_mx(a.data_ptr(), b.data_ptr(), out.data_ptr(), M, N, K, sfa_blocked.data_ptr(),
-                                   sfb_blocked.data_ptr(), _ptr(scale_a), _ptr(scale_b), _stream_handle(stream))
-    check(rc, "hgemm_fp8_tn_mx")
+        rc = lib().hgemm_fp8_tn_mx_config(a.data_ptr(), b.data_ptr(), out.data_ptr(), M, N, K,
+                                          sfa_blocked.data_ptr(), sfb_blocked.data_ptr(), _ptr(scale_a),
+                                          _ptr(scale_b), config, _stream_handle(stream))
+    check(rc, "hgemm_fp8_tn_mx_config")
     return out

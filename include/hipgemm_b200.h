@@ -185,6 +185,13 @@ const char* hgemm_version(void);
  * this is that instruction with scales in use. */
 int hgemm_fp8_tn_mx(const void* A, const void* B, void* C, int M, int N, int K, const void* SFA, const void* SFB,
                     const float* d_scale_a, const float* d_scale_b, hgemm_stream_t stream);
+/* hgemm_fp8_tn_mx with its kernel chosen: 0 = by wave count (what hgemm_fp8_tn_mx does),
+ * 1 = 128 x 256 tiles, one accumulator; 2 = 128 x 128 tiles.  Names: hgemm_mx_config_name. */
+int hgemm_fp8_tn_mx_config(const void* A, const void* B, void* C, int M, int N, int K, const void* SFA,
+                           const void* SFB, const float* d_scale_a, const float* d_scale_b, int config,
+                           hgemm_stream_t stream);
+int hgemm_mx_num_configs(void);
+const char* hgemm_mx_config_name(int config);
 /* Bytes of a blocked scale-factor tensor for `rows` rows and K columns. */
 size_t hgemm_mx_sf_bytes(int rows, int K);
 /* Row-major (rows x K/32) e8m0 bytes -> the blocked layout above (host memory). */

@@ -144,3 +144,21 @@ def test_from_host_argument_checks():
     assert L.hgemm_fp8_tn_from_host(*args, 8, 8, 24, None, FAKE, FAKE, FAKE, None, None) == hg.HGEMM_ERR_ALIGNMENT
     assert L.hgemm_fp8_tn_from_host(*args, 8, 8, 16, FAKE, FAKE, FAKE, FAKE, None, None) == hg.HGEMM_ERR_INVALID_VALUE
     assert L.hgemm_fp8_tn_from_host(*args, 0, 8, 16, None, None, None, None, None, None) == hg.HGEMM_OK
+
+
+def test_mx_argument_checks():
+    L = hg.lib()
+    sf = FAKE
+    assert L.hgemm_mx_num_configs() == 3
+    assert [L.hgemm_mx_config_name(c).decode() for c in range(3)] == ["auto", "mx_bn256_s4", "mx_bn128_s5"]
+    assert L.hgemm_mx_config_name(3) is None and L.hgemm_mx_config_name(-1) is None
+    run = L.hgemm_fp8_tn_mx_config
+    assert run(FAKE, FAKE, FAKE, 8, 8, 64, sf, sf, None, None, 3, None) == hg.HGEMM_ERR_INVALID_VALUE
+    assert run(FAKE, FAKE, FAKE, 8, 8, 64, sf, sf, None, None, -1, None) == hg.HGEMM_ERR_INVALID_VALUE
+    assert run(FAKE, FAKE, FAKE, 8, 8, 48, sf, sf, None, None, 0, None) == hg.HGEMM_ERR_ALIGNMENT   # K % 32
+    assert run(FAKE, FAKE, FAKE, 8, 8, 64, None, sf, None, None, 0, None) == hg.HGEMM_ERR_INVALID_VALUE
+    assert run(FAKE, FAKE, FAKE, 8, 8, 64, sf + 4, sf, None, None, 0, None) == hg.HGEMM_ERR_ALIGNMENT
+    assert run(FAKE, FAKE, FAKE, 8, 12, 64, sf, sf, None, None, 0, None) == hg.HGEMM_ERR_ALIGNMENT  # N % 8
+    assert L.hgemm_fp8_tn_mx(FAKE, FAKE, FAKE, 0, 8, 64, None, None, None, None, None) == hg.HGEMM_OK
+    assert L.hgemm_mx_sf_bytes(300, 1056) == 3 * 9 * 512 and L.hgemm_mx_sf_bytes(0, 64) == 0
+    assert L.hgemm_host_mx_sf_to_blocked(FAKE, 4, 48, FAKE) == hg.HGEMM_ERR_INVALID_VALUE

@@ -43,9 +43,10 @@ def _mx_operand(rows, K, seed):
     return oracle.quantize_mx(x)
 
 
+@pytest.mark.parametrize("config", [1, 2])
 @pytest.mark.parametrize("M,N,K", [(128, 128, 128), (256, 384, 1024), (300, 520, 1056), (1000, 1032, 2080),
                                    (4096, 4096, 4096)])
-def test_mx_gemm_matches_oracle(cuda_device, M, N, K):
+def test_mx_gemm_matches_oracle(cuda_device, M, N, K, config):
     import hipgemm_b200 as hg
     A, SFA = _mx_operand(M, K, M)
     B, SFB = _mx_operand(N, K, N + 1)
@@ -53,7 +54,7 @@ def test_mx_gemm_matches_oracle(cuda_device, M, N, K):
     sfb = hg.mx_sf_to_blocked(torch.from_numpy(SFB), K).cuda()
     sa = torch.tensor([0.75], dtype=torch.float32, device="cuda")
     sb = torch.tensor([1.5], dtype=torch.float32, device="cuda")
-    c = hg.fp8_gemm_tn_mx(torch.from_numpy(A).cuda(), torch.from_numpy(B).cuda(), sfa, sfb, sa, sb)
+    c = hg.fp8_gemm_tn_mx(torch.from_numpy(A).cuda(), torch.from_numpy(B).cuda(), sfa, sfb, sa, sb, config=config)
     torch.cuda.synchronize()
     assert hg.device_status() == 0
     got = c_bits(c)
@@ -78,11 +79,33 @@ def test_mx_unit_scales_equal_plain_gemm(cuda_device):
     ones_a = hg.mx_sf_to_blocked(torch.full((M, K // 32), 127, dtype=torch.uint8), K).cuda()
     ones_b = hg.mx_sf_to_blocked(torch.full((N, K // 32), 127, dtype=torch.uint8), K).cuda()
     a, b = torch.from_numpy(A).cuda(), torch.from_numpy(B).cuda()
-    mx = hg.fp8_gemm_tn_mx(a, b, ones_a, ones_b)
     plain = hg.fp8_gemm_tn(a, b)
     ref = oracle.gemm(A, B)
-    assert oracle.validate(c_bits(mx), ref)[0] == 0
     assert oracle.validate(c_bits(plain), ref)[0] == 0
+    for config in (0, 1, 2):
+        mx = hg.fp8_gemm_tn_mx(a, b, ones_a, ones_b, config=config)
+        assert oracle.validate(c_bits(mx), ref)[0] == 0, config
+
+
+def test_mx_repeated_calls_identical(cuda_device):
+    """Deterministic: same bits on every call (no split-K, fixed MMA order), both kernels,
+    with tiles queued several deep per CTA so the one-accumulator hand-off is exercised."""
+    import hipgemm_b200 as hg
+    M, N, K = 4096, 8192, 1024
+    A, SFA = _mx_operand(M, K, 11)
+    B, SFB = _mx_operand(N, K, 12)
+    a, b = torch.from_numpy(A).cuda(), torch.from_numpy(B).cuda()
+    sfa = hg.mx_sf_to_blocked(torch.from_numpy(SFA), K).cuda()
+    sfb = hg.mx_sf_to_blocked(torch.from_numpy(SFB), K).cuda()
+    for config in (1, 2):
+        first = hg.fp8_gemm_tn_mx(a, b, sfa, sfb, config=config)
+        for _ in range(3):
+            assert torch.equal(hg.fp8_gemm_tn_mx(a, b, sfa, sfb, config=config).view(torch.int16),
+                               first.view(torch.int16))
+    rows = sample_rows(M, 24)
+    ref = np.concatenate([oracle.gemm_mx(A, B, SFA, SFB, 1.0, 1.0, r, r + 1) for r in rows])
+    bad, info = _mismatches(np.ascontiguousarray(c_bits(first)[rows]), ref, _abs_products(A, B, SFA, SFB, rows, 1.0))
+    assert bad == 0, info
 
 
 def test_mx_argument_checks(cuda_device):

@@ -61,6 +61,7 @@ def parse_args():
     ap.add_argument("--allgather", action="store_true", help="also time the NCCL all-gather of C (N > 1)")
     ap.add_argument("--no-cublas", action="store_true", help="skip the cuBLASLt comparison leg")
     ap.add_argument("--no-cpu", action="store_true", help="skip the CPU baseline leg")
+    ap.add_argument("--no-mx", action="store_true", help="skip the MX block-scaled GEMM and quantiser legs")
     ap.add_argument("--seed", type=int, default=0)
     return ap.parse_args()
 
@@ -228,6 +229,61 @@ def quantize_on_device(x, group=None):
     return q.view(torch.uint8), scale
 
 
+def mx_legs(args, hg, m, N, K, std_b, rank, dev, timed, peak, hbm_peak, C, no_cublas=False) -> dict:
+    """OCP MX (e8m0 scale per 32 K elements) on this rank's GEMM shape: the device MX
+    quantiser (fp32 -> e4m3 + blocked scales) and the block-scaled GEMM over rotating input
+    sets larger than L2, with cuBLASLt's block-scaled torch._scaled_mm on the same bytes."""
+    import torch
+
+    set_bytes = m * K + N * K
+    nset = int(min(16, max(2, math.ceil(4 * L2_BYTES / set_bytes))))
+    A, B, SA, SB = [], [], [], []
+    for j in range(nset):
+        g = torch.Generator(device=dev)
+        g.manual_seed(args.seed + 2 * j * 1000003 + 7919 * rank + 17)
+        qa, sa = hg.quantize_mx_e4m3(torch.randn((m, K), generator=g, device=dev, dtype=torch.float32))
+        g.manual_seed(args.seed + 2 * j * 1000003 + 18)
+        qb, sb = hg.quantize_mx_e4m3(torch.randn((N, K), generator=g, device=dev, dtype=torch.float32) * std_b)
+        A.append(qa); B.append(qb); SA.append(sa); SB.append(sb)
+    torch.cuda.synchronize()
+    flops = 2.0 * m * N * K
+    ms_mx, _ = timed(lambda i: hg.fp8_gemm_tn_mx(A[i % nset], B[i % nset], SA[i % nset], SB[i % nset], out=C),
+                     max(5, min(args.steps, 100)), max(3, args.warmup))
+    if hg.device_status() != 0:
+        raise SystemExit("MX kernel status word set: a bounded wait expired")
+    out = {"mx_gemm": {
+        "what": "OCP MX e4m3 block-scaled GEMM (tcgen05 kind::mxf8f6f4.block_scale), e8m0 scale per 32 K, "
+                "inputs quantised on the device from N(0,1) by hgemm_quantize_mx_e4m3",
+        "value": flops / (ms_mx * 1e-3) / 1e12, "unit": "TFLOP/s", "ms_per_step": ms_mx,
+        "frac": flops / (ms_mx * 1e-3) / 1e12 / peak, "peak": peak,
+        "l2": f"rotating inputs: {nset} sets > 126 MB L2"}}
+    if not no_cublas:
+        try:
+            e8 = torch.float8_e8m0fnu
+
+            def lt(i):
+                j = i % nset
+                torch._scaled_mm(A[j].view(torch.float8_e4m3fn), B[j].view(torch.float8_e4m3fn).t(),
+                                 scale_a=SA[j].view(e8), scale_b=SB[j].view(e8), out_dtype=torch.bfloat16)
+            ms_lt, _ = timed(lt, max(5, min(args.steps, 100)), 3)
+            out["cublaslt_mx"] = {"value": flops / (ms_lt * 1e-3) / 1e12, "unit": "TFLOP/s", "ms_per_step": ms_lt,
+                                  "what": "torch._scaled_mm with e8m0 block scales (cuBLASLt), same bytes"}
+        except Exception as e:  # a torch build without block-scaled _scaled_mm on this GPU
+            out["cublaslt_mx"] = {"unavailable": f"{type(e).__name__}: {str(e).splitlines()[0][:160]}"}
+    del A, B, SA, SB
+    x = torch.randn((m, K), device=dev, dtype=torch.float32)
+    q = torch.empty((m, K), dtype=torch.uint8, device=dev)
+    sf = torch.empty(int(hg.lib().hgemm_mx_sf_bytes(m, K)), dtype=torch.uint8, device=dev)
+    ms_q, _ = timed(lambda i: hg.quantize_mx_e4m3(x, out=q, sf_out=sf), max(5, min(args.steps, 50)), 3)
+    q_bytes = m * K * (4.0 + 1.0 + 1.0 / 32)  # read fp32 once, write e4m3 and one scale per 32
+    out["mx_quantizer"] = {
+        "what": "hgemm_quantize_mx_e4m3 fp32 -> e4m3 + blocked e8m0 scales, on this rank's A shape",
+        "ms_per_call": ms_q, "achieved_gbs": q_bytes / (ms_q * 1e-3) / 1e9, "peak_gbs": hbm_peak[0],
+        "frac": q_bytes / (ms_q * 1e-3) / 1e9 / hbm_peak[0], "peak_source": hbm_peak[1],
+        "algorithmic_bytes": q_bytes}
+    return out
+
+
 def run_ours(args) -> None:
     import torch
     import torch.distributed as dist
@@ -341,6 +397,9 @@ def run_ours(args) -> None:
         "frac": q_bytes / (ms_q * 1e-3) / 1e9 / hbm_peak[0], "peak_source": hbm_peak[1],
         "algorithmic_bytes": q_bytes, "moved_bytes": 9.0 * m * K}
     del xq, qq
+
+    if not args.no_mx:
+        extra.update(mx_legs(args, hg, m, N, K, std_b, rank, dev, timed, peak, hbm_peak, C, no_cublas=args.no_cublas))
 
     # End to end through the public API: pinned host A/B in, GEMM, C back to pinned host.
     hA = A[0].cpu().pin_memory()

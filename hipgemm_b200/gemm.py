@@ -223,3 +223,32 @@ def fp8_gemm_tn_mx(a: torch.Tensor, b: torch.Tensor, sfa_blocked: torch.Tensor, 
                                           _ptr(scale_b), config, _stream_handle(stream))
     check(rc, "hgemm_fp8_tn_mx_config")
     return out
+
+
+def quantize_mx_e4m3(x: torch.Tensor, out: torch.Tensor | None = None, sf_out: torch.Tensor | None = None,
+                     stream: torch.cuda.Stream | None = None) -> tuple[torch.Tensor, torch.Tensor]:
+    """OCP MX e4m3 quantisation on the GPU (hgemm_quantize_mx_e4m3) of a rows x K fp32 or bf16
+    tensor: returns (q, sf_blocked), q the e4m3 bits (uint8, x's shape) and sf_blocked the
+    e8m0 scales in the layout fp8_gemm_tn_mx takes (also torch._scaled_mm's blocked e8m0
+    layout)."""
+    if not x.is_cuda or not x.is_contiguous() or x.dim() != 2:
+        raise ValueError("x must be a contiguous 2-D CUDA tensor (there is no CPU path)")
+    if x.dtype == torch.float32:
+        dt = 0
+    elif x.dtype == torch.bfloat16:
+        dt = 1
+    else:
+        raise TypeError(f"x must be float32 or bfloat16, got {x.dtype}")
+    rows, K = x.shape
+    sf_bytes = int(lib().hgemm_mx_sf_bytes(rows, K))
+    q = torch.empty((rows, K), dtype=torch.uint8, device=x.device) if out is None else out
+    sf = torch.empty(sf_bytes, dtype=torch.uint8, device=x.device) if sf_out is None else sf_out
+    if q.numel() != x.numel() or q.dtype != torch.uint8 or not q.is_contiguous() or q.device != x.device:
+        raise ValueError("out must be a contiguous uint8 tensor with x's size on x's device")
+    if sf.numel() < sf_bytes or sf.dtype != torch.uint8 or not sf.is_contiguous() or sf.device != x.device:
+        raise ValueError(f"sf_out must be a contiguous uint8 tensor of {sf_bytes} bytes on x's device")
+    with torch.cuda.device(x.device):
+        rc = lib().hgemm_quantize_mx_e4m3(x.data_ptr(), dt, rows, K, q.data_ptr(), sf.data_ptr(),
+                                          _stream_handle(stream))
+    check(rc, "hgemm_quantize_mx_e4m3")
+    return q, sf

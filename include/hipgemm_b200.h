@@ -212,6 +212,16 @@ int hgemm_host_mx_sf_to_blocked(const uint8_t* sf, int rows, int K, uint8_t* blo
  * quantiser moved onto the GPU. */
 int hgemm_quantize_e4m3(const void* x, int x_dtype, size_t n, void* q, float* d_scale, hgemm_stream_t stream);
 
+/* OCP MX e4m3 quantiser on the device: x (rows x K, fp32 or bf16 by x_dtype, row-major) ->
+ * q (rows x K e4m3 bytes) and one e8m0 scale per 32 elements of a row, written in the
+ * blocked layout hgemm_fp8_tn_mx reads (hgemm_mx_sf_bytes(rows, K) bytes; padding = 127).
+ * X = floor(log2(amax)) - 8 clamped to [-127, 127] (-127 for a block whose amax is 0,
+ * subnormal or infinite; NaNs do not count), scale byte X + 127, q = e4m3_satfinite(x * 2^-X).
+ * K % 32 == 0 (HGEMM_ERR_ALIGNMENT); x and q 16-byte aligned; fewer than 2^32 blocks of 32
+ * (HGEMM_ERR_UNSUPPORTED otherwise: 275 GB of bf16).  Stream-ordered, no sync. */
+int hgemm_quantize_mx_e4m3(const void* x, int x_dtype, int rows, int K, void* q, void* sf_blocked,
+                           hgemm_stream_t stream);
+
 /* ---- host utilities mirroring the reference harness (utils.hpp) ---------------------- */
 
 /* utils.hpp:27-33 init_random, generalised: std::mt19937(seed) feeding

@@ -162,3 +162,16 @@ def test_mx_argument_checks():
     assert L.hgemm_fp8_tn_mx(FAKE, FAKE, FAKE, 0, 8, 64, None, None, None, None, None) == hg.HGEMM_OK
     assert L.hgemm_mx_sf_bytes(300, 1056) == 3 * 9 * 512 and L.hgemm_mx_sf_bytes(0, 64) == 0
     assert L.hgemm_host_mx_sf_to_blocked(FAKE, 4, 48, FAKE) == hg.HGEMM_ERR_INVALID_VALUE
+
+
+def test_mx_quantiser_argument_checks():
+    L = hg.lib()
+    q = L.hgemm_quantize_mx_e4m3
+    assert q(FAKE, 2, 4, 64, FAKE, FAKE, None) == hg.HGEMM_ERR_INVALID_VALUE     # dtype
+    assert q(FAKE, 0, -1, 64, FAKE, FAKE, None) == hg.HGEMM_ERR_INVALID_VALUE    # rows
+    assert q(FAKE, 0, 4, 48, FAKE, FAKE, None) == hg.HGEMM_ERR_ALIGNMENT         # K % 32
+    assert q(None, 0, 4, 64, FAKE, FAKE, None) == hg.HGEMM_ERR_INVALID_VALUE
+    assert q(FAKE, 0, 4, 64, FAKE, None, None) == hg.HGEMM_ERR_INVALID_VALUE
+    assert q(FAKE + 8, 1, 4, 64, FAKE, FAKE, None) == hg.HGEMM_ERR_ALIGNMENT
+    assert q(FAKE, 0, 4, 64, FAKE + 4, FAKE, None) == hg.HGEMM_ERR_ALIGNMENT
+    assert q(None, 0, 0, 64, None, None, None) == hg.HGEMM_OK                    # nothing to do

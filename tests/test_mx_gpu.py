@@ -115,3 +115,42 @@ def test_mx_argument_checks(cuda_device):
     with pytest.raises(hg.HgemmError) as e:
         hg.fp8_gemm_tn_mx(a, a, sf, sf)  # K % 32 != 0
     assert e.value.code == hg.HGEMM_ERR_ALIGNMENT
+
+
+def test_mx_matches_cublaslt_block_scaled(cuda_device):
+    """Same bytes through cuBLASLt's block-scaled GEMM (torch._scaled_mm with e8m0 scales,
+    whose blocked scale layout is this library's): both must meet the oracle's tolerance,
+    and agree with each other to bf16 rounding almost everywhere."""
+    import hipgemm_b200 as hg
+    M, N, K = 1024, 1536, 2048
+    xa = torch.from_numpy(oracle.normal_f32(M * K, seed=21).reshape(M, K)).cuda()
+    xb = torch.from_numpy(oracle.normal_f32(N * K, seed=22).reshape(N, K)).cuda()
+    qa, sfa = hg.quantize_mx_e4m3(xa)
+    qb, sfb = hg.quantize_mx_e4m3(xb)
+    try:
+        lt = torch._scaled_mm(qa.view(torch.float8_e4m3fn), qb.view(torch.float8_e4m3fn).t(),
+                              scale_a=sfa.view(torch.float8_e8m0fnu), scale_b=sfb.view(torch.float8_e8m0fnu),
+                              out_dtype=torch.bfloat16)
+    except Exception as e:  # no block-scaled _scaled_mm in this torch build
+        pytest.skip(f"torch._scaled_mm block-scaled unavailable: {e}")
+    ours = hg.fp8_gemm_tn_mx(qa, qb, sfa, sfb)
+    torch.cuda.synchronize()
+    rows = sample_rows(M, 32)
+    A_np, B_np = qa.cpu().numpy(), qb.cpu().numpy()
+    SFA = _rowmajor_sf(sfa.cpu().numpy(), M, K)
+    SFB = _rowmajor_sf(sfb.cpu().numpy(), N, K)
+    ref = np.concatenate([oracle.gemm_mx(A_np, B_np, SFA, SFB, 1.0, 1.0, r, r + 1) for r in rows])
+    absum = _abs_products(A_np, B_np, SFA, SFB, rows, 1.0)
+    assert _mismatches(np.ascontiguousarray(c_bits(ours)[rows]), ref, absum)[0] == 0
+    assert _mismatches(np.ascontiguousarray(c_bits(lt)[rows]), ref, absum)[0] == 0
+    d = (ours.float() - lt.float()).abs()
+    assert float((d > 1e-2 * lt.float().abs() + 1e-3).float().mean()) < 1e-3
+
+
+def _rowmajor_sf(blocked: np.ndarray, rows: int, K: int) -> np.ndarray:
+    """Inverse of the blocked layout (for reading device scales back into the oracle)."""
+    groups, k_atoms = K // 32, (K + 127) // 128
+    r = np.arange(rows)[:, None]
+    g = np.arange(groups)[None, :]
+    idx = ((r // 128) * k_atoms + g // 4) * 512 + 16 * (r % 32) + 4 * ((r // 32) % 4) + g % 4
+    return blocked[idx]

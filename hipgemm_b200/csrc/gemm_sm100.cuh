@@ -61,13 +61,23 @@ struct GemmParams {
     int sk_slots;
     float* partials;  // [slot][piece 0/1][cta][128 x BN] fp32 (layout: partial_offset)
     int* counters;    // [sk tile][cta]; zero on entry, left zero on exit
-    // MX block scaling (the MX kernel only): e8m0 scale factors, one per 32 K elements of a
+    // MX block scaling (the MX kernels only): e8m0 scale factors, one per 32 K elements of a
     // row, in 512-byte atoms of 128 rows x 4 K-groups (byte 16*(r%32) + 4*(r/32) + g),
-    // atom (row block i, K block j) at offset (i * sf_k_atoms + j) * 512.
-    const uint8_t* sfa;
-    const uint8_t* sfb;
+    // atom (row block i, K block j) at offset (i * sf_k_atoms + j) * 512, read through the
+    // SfMaps tensor maps.
     int sf_k_atoms;
 };
+
+// MX scale factors as 3-D TMA tensors over the blocked bytes: x = 128 bytes, y = 128-byte
+// rows along K (4 per 512-byte atom, 4 * ceil(K/128) per row block), z = 128-row block
+// (stride ceil(K/128) * 512 bytes).  A box of 4 rows by 1 (A) or BN / 128 (B) row blocks
+// fetches one K block's atoms in one load; blocks past M or N read as zeros (the MX kernels
+// only; zero otherwise).
+struct SfMaps {
+    CUtensorMap a;
+    CUtensorMap b;
+};
+constexpr int kSfRowsPerAtom = 4;
 
 // Extra outputs for the fused all-gather: the same C rows on other GPUs (peer memory
 // mapped into this process), written by TMA stores of the same staged tiles.
@@ -204,14 +214,6 @@ __device__ __forceinline__ void st_global_v4(float* p, float a, float b, float c
     asm volatile("st.global.v4.f32 [%0], {%1, %2, %3, %4};" ::"l"(p), "f"(a), "f"(b), "f"(c), "f"(d) : "memory");
 }
 
-// Scale-factor atoms (128 rows of B each) that column block nb of width 128 * ATOMS covers
-// inside N: ATOMS except for a last block that ends within the tile.
-template <int ATOMS>
-__device__ __forceinline__ int sfb_atoms_in_tile(const GemmParams& p, int nb) {
-    const int left = (p.N + 127) / 128 - nb * ATOMS;
-    return left < ATOMS ? left : ATOMS;
-}
-
 template <int CTAS, int BN, int STAGES, bool MX = false>
 struct KernelShape {
     static constexpr int BM = 128 * CTAS;   // output tile rows
@@ -235,7 +237,10 @@ struct KernelShape {
     static constexpr int OFF_A = 0;
     static constexpr int OFF_B = OFF_A + STAGES * A_BYTES;
     static constexpr int OFF_EPI = OFF_B + STAGES * B_BYTES;
-    // MX: per stage, one 512-byte scale-factor atom for A's 128 rows and one per 128 rows of B.
+    // MX: per stage, with the operands and on the same barriers (scale factors are
+    // latency-bound: they need the stage ring's full depth), one 512-byte atom for this
+    // CTA's 128 rows of A, then one per 128 columns of the whole tile (a pair's CTAs both
+    // hold all of B's): two loads per stage.
     static constexpr int SFB_ATOMS = (BN + 127) / 128;
     static constexpr int SF_BYTES = MX ? 512 * (1 + SFB_ATOMS) : 0;
     static constexpr int OFF_SF = OFF_EPI + 4 * 2 * EPI_BUF_BYTES;
@@ -253,7 +258,6 @@ struct KernelShape {
     static constexpr uint32_t IDESC = idesc_e4m3_f32(BM, BN);
     static constexpr int PARTIAL_FLOATS = 128 * BN;  // one CTA's share of a partial tile
     static_assert(CTAS == 1 || CTAS == 2, "one CTA or a CTA pair");
-    static_assert(!MX || CTAS == 1, "MX block scaling is built for the single-CTA tile");
     static_assert(!MX || BN % 128 == 0, "MX tiles cover whole 128-row scale-factor atoms of B");
     static_assert(COLS_USED <= 512, "tensor memory holds 512 columns");
     static_assert(BN % 32 == 0 && BN >= 64 && BN <= 256, "BN must be a multiple of 32 in [64, 256]");
@@ -267,7 +271,7 @@ template <int CTAS, int BN, int STAGES, bool MX = false>
 __global__ void __launch_bounds__(192, 1)
     fp8_gemm_tn_sm100(const __grid_constant__ CUtensorMap tm_a, const __grid_constant__ CUtensorMap tm_b,
                       const __grid_constant__ CUtensorMap tm_c, const GemmParams p,
-                      const __grid_constant__ PeerOutputs peers) {
+                      const __grid_constant__ PeerOutputs peers, const __grid_constant__ SfMaps sfm) {
     using S = KernelShape<CTAS, BN, STAGES, MX>;
     extern __shared__ uint8_t smem_raw[];
     // 128-byte swizzle atoms need 1024-byte alignment.
@@ -308,6 +312,10 @@ __global__ void __launch_bounds__(192, 1)
         prefetch_tmap(&tm_a);
         prefetch_tmap(&tm_b);
         prefetch_tmap(&tm_c);
+        if constexpr (MX) {
+            prefetch_tmap(&sfm.a);
+            prefetch_tmap(&sfm.b);
+        }
     }
     if (warp == 1) {
         tmem_alloc<CTAS>(tmem_slot, S::TMEM_COLS);  // for a pair: collective with the peer's warp 1
@@ -347,33 +355,31 @@ __global__ void __launch_bounds__(192, 1)
                     }
                     const uint32_t a_dst = base + S::OFF_A + stage * S::A_BYTES;
                     const uint32_t b_dst = base + S::OFF_B + stage * S::B_BYTES;
+                    // MX: this K block's scale factors, A's for this CTA's 128 rows and B's for
+                    // all of the tile's columns (full boxes: rows past M or N read as zeros).
+                    const uint32_t sf_dst = base + S::OFF_SF + stage * S::SF_BYTES;
+                    const int a_blk = mb * CTAS + static_cast<int>(rank);
+                    const int b_blk = nb * S::SFB_ATOMS;
+                    const int sf_y = kb * kSfRowsPerAtom;
                     if (leader) {
                         // For a pair: the MMAs that read this stage finished in both CTAs.
                         if (kPair && !first_pass) mbar_arrive_cluster(peer_empty0 + 8 * stage);
                         const uint32_t full = bar_full + 8 * stage;
-                        // MX: B's 128-row scale-factor atoms of this tile that exist (a tile
-                        // wider than the rest of N has fewer; its columns past N are clipped).
-                        const int sfb_atoms = MX ? sfb_atoms_in_tile<S::SFB_ATOMS>(p, nb) : 0;
-                        mbar_arrive_expect_tx(full, CTAS * S::STAGE_BYTES + (MX ? 512 * (1 + sfb_atoms) : 0));
+                        mbar_arrive_expect_tx(full, CTAS * (S::STAGE_BYTES + S::SF_BYTES));
                         tma_load_2d(a_dst, &tm_a, kb * S::BK, a_row, full);
                         tma_load_2d(b_dst, &tm_b, kb * S::BK, b_row, full);
                         if constexpr (MX) {
-                            // This K block's scale-factor atoms: A's row block mb, B's
-                            // 128-row blocks of column block nb.
-                            const uint32_t sf_dst = base + S::OFF_SF + stage * S::SF_BYTES;
-                            const size_t ka = static_cast<size_t>(p.sf_k_atoms);
-                            bulk_load_1d(sf_dst, p.sfa + (static_cast<size_t>(mb) * ka + kb) * 512, 512, full);
-#pragma unroll
-                            for (int i = 0; i < S::SFB_ATOMS; ++i) {
-                                if (i >= sfb_atoms) break;
-                                const size_t rb = static_cast<size_t>(nb) * S::SFB_ATOMS + i;
-                                bulk_load_1d(sf_dst + 512 * (1 + i), p.sfb + (rb * ka + kb) * 512, 512, full);
-                            }
+                            tma_load_3d(sf_dst, &sfm.a, 0, sf_y, a_blk, full);
+                            tma_load_3d(sf_dst + 512, &sfm.b, 0, sf_y, b_blk, full);
                         }
                     } else {
                         const uint32_t full = full_leader0 + 8 * stage;
                         tma_load_2d_pair(a_dst, &tm_a, kb * S::BK, a_row, full);
                         tma_load_2d_pair(b_dst, &tm_b, kb * S::BK, b_row, full);
+                        if constexpr (MX) {
+                            tma_load_3d_pair(sf_dst, &sfm.a, 0, sf_y, a_blk, full);
+                            tma_load_3d_pair(sf_dst + 512, &sfm.b, 0, sf_y, b_blk, full);
+                        }
                     }
                     if (++stage == STAGES) {
                         stage = 0;
@@ -393,6 +399,16 @@ __global__ void __launch_bounds__(192, 1)
             int acc = 0;
             uint32_t acc_phase = 0;
             bool ok = true;
+            // MX: the scale factors of stage s go to its own tensor-memory columns with
+            // tcgen05.cp, which runs in issue order with the MMAs that read them.
+            auto issue_sf_cp = [&](int s) {
+                const uint32_t tsfa = tmem_base + static_cast<uint32_t>(S::OFF_SF_COL + s * S::SF_COLS);
+                const uint32_t sf_src = base + S::OFF_SF + s * S::SF_BYTES;
+#pragma unroll
+                for (int i = 0; i <= S::SFB_ATOMS; ++i) {
+                    tmem_cp_32x128b_warpx4<CTAS>(tsfa + 4 * i, sf_smem_desc(sf_src + 512 * i));
+                }
+            };
             Work w;
             for (int idx = 0; ok && get_work(p, slot, nslots, idx, w); ++idx) {
                 if (!mbar_wait<kPair>(bar_tempty + 8 * acc, acc_phase ^ 1u, abort_flag, kErrMmaTmemEmpty)) {
@@ -401,8 +417,6 @@ __global__ void __launch_bounds__(192, 1)
                 }
                 tc_fence_after();
                 const uint32_t d_tmem = tmem_base + static_cast<uint32_t>(acc * BN);
-                int mma_mb = 0, mma_nb = 0;
-                if constexpr (MX) tile_coords(w.tile, p, mma_mb, mma_nb);
                 for (int kb = w.kb_begin; kb < w.kb_end; ++kb) {
                     if (!mbar_wait<kPair>(bar_full + 8 * stage, phase, abort_flag, kErrMmaFull)) {
                         ok = false;
@@ -412,25 +426,17 @@ __global__ void __launch_bounds__(192, 1)
                     const uint64_t a_desc = sw128_kmajor_desc(base + S::OFF_A + stage * S::A_BYTES);
                     const uint64_t b_desc = sw128_kmajor_desc(base + S::OFF_B + stage * S::B_BYTES);
                     if constexpr (MX) {
-                        // Scale factors of this stage into its tensor-memory columns: A's at
-                        // tsfa (4 columns), B's after them; the MMAs below read them in order.
+                        // Scale factors of this stage: A's at tsfa (4 columns), B's after them.
                         const uint32_t tsfa = tmem_base + static_cast<uint32_t>(S::OFF_SF_COL + stage * S::SF_COLS);
                         const uint32_t tsfb = tsfa + 4;
-                        const uint32_t sf_src = base + S::OFF_SF + stage * S::SF_BYTES;
-                        tmem_cp_32x128b_warpx4(tsfa, sf_smem_desc(sf_src));
-                        const int sfb_atoms = sfb_atoms_in_tile<S::SFB_ATOMS>(p, mma_nb);
-#pragma unroll
-                        for (int i = 0; i < S::SFB_ATOMS; ++i) {
-                            if (i >= sfb_atoms) break;
-                            tmem_cp_32x128b_warpx4(tsfb + 4 * i, sf_smem_desc(sf_src + 512 * (1 + i)));
-                        }
+                        issue_sf_cp(stage);
 #pragma unroll
                         for (int k = 0; k < S::BK / S::UMMA_K; ++k) {
                             const uint64_t koff = static_cast<uint64_t>((k * S::UMMA_K) >> 4);
                             const uint32_t accumulate = (kb > w.kb_begin || k > 0) ? 1u : 0u;
                             // K slice k uses byte k of each scale-factor column.
                             const uint32_t sf_id = static_cast<uint32_t>(k);
-                            mma_mxf8f6f4(d_tmem, a_desc + koff, b_desc + koff, idesc_mx_e4m3(S::BM, BN, sf_id),
+                            mma_mxf8f6f4<CTAS>(d_tmem, a_desc + koff, b_desc + koff, idesc_mx_e4m3(S::BM, BN, sf_id),
                                          tsfa | (sf_id << 30), tsfb | (sf_id << 30), accumulate);
                         }
                     } else {

@@ -35,6 +35,7 @@ struct DeviceState {
     // CTA pairs this comes from cudaOccupancyMaxActiveClusters, which can be below
     // num_sms / 2 (clusters must fit inside one GPC).
     int resident_ctas[kMaxConfigs] = {};
+    int mx_resident_ctas[kMaxConfigs] = {};  // the same for the MX configurations
     cudaMemPool_t pool = nullptr;  // stream-K workspaces
 };
 
@@ -58,12 +59,12 @@ struct KernelConfig {
     int epi_cols;        // columns per C store box (64: 128-byte swizzle, 32: 64-byte swizzle)
     const void* kernel;  // __global__ function pointer
     int (*launch)(const CUtensorMap&, const CUtensorMap&, const CUtensorMap&, const GemmParams&,
-                  const PeerOutputs&, int grid, cudaStream_t);
+                  const PeerOutputs&, const SfMaps&, int grid, cudaStream_t);
 };
 
 template <int CTAS, int BN, int STAGES, bool MX = false>
 int launch_kernel(const CUtensorMap& ta, const CUtensorMap& tb, const CUtensorMap& tc, const GemmParams& p,
-                  const PeerOutputs& peers, int grid, cudaStream_t stream) {
+                  const PeerOutputs& peers, const SfMaps& sfm, int grid, cudaStream_t stream) {
     using S = KernelShape<CTAS, BN, STAGES, MX>;
     cudaLaunchConfig_t cfg{};
     cfg.gridDim = dim3(static_cast<unsigned>(grid), 1, 1);
@@ -77,7 +78,8 @@ int launch_kernel(const CUtensorMap& ta, const CUtensorMap& tb, const CUtensorMa
     attr[0].val.clusterDim.z = 1;
     cfg.attrs = attr;
     cfg.numAttrs = CTAS == 2 ? 1 : 0;
-    const cudaError_t e = cudaLaunchKernelEx(&cfg, fp8_gemm_tn_sm100<CTAS, BN, STAGES, MX>, ta, tb, tc, p, peers);
+    const cudaError_t e =
+        cudaLaunchKernelEx(&cfg, fp8_gemm_tn_sm100<CTAS, BN, STAGES, MX>, ta, tb, tc, p, peers, sfm);
     return e == cudaSuccess ? HGEMM_OK : HGEMM_ERR_CUDA;
 }
 
@@ -104,27 +106,30 @@ const KernelConfig kConfigs[] = {
 };
 constexpr int kNumConfigs = sizeof(kConfigs) / sizeof(kConfigs[0]);
 
-// MX block-scaled kernels (index 1 and 2 of hgemm_fp8_tn_mx_config; 0 = choose).
-// 128 x 256 tiles with one accumulator (early release), and 128 x 128 tiles with two for
-// grids too small to fill the GPU with the wide tile.  eff: measured throughput at 8192^3
-// relative to the dense peak of the plain kernel's best config.
+// MX block-scaled kernels (index c + 1 of hgemm_fp8_tn_mx_config; 0 = choose).  256 x 256
+// tiles on CTA pairs and 128 x 256 tiles, both with one accumulator (early release), and
+// 128 x 128 tiles with two for grids too small to fill the GPU with the wide tiles.  eff:
+// measured per-SM throughput at 8192^3 relative to the best config.
 const KernelConfig kMxConfigs[] = {
     make_config<1, 256, 4, true>("mx_bn256_s4", 0.90),
     make_config<1, 128, 5, true>("mx_bn128_s5", 0.52),
+    make_config<2, 256, 6, true>("mx_pair256_s6", 1.0),
 };
 constexpr int kNumMxConfigs = sizeof(kMxConfigs) / sizeof(kMxConfigs[0]);
 
-// Fewest estimated tile-time units: waves of tiles over the SMs times the tile's MMA work
-// (BN / 128) over its efficiency.
-int choose_mx_config(int M, int N, int num_sms) {
+// Fewest estimated tile-time units: waves of tiles over the resident slots (CTAs or CTA
+// pairs) times the tile's per-SM MMA work (BM * BN / (128 * 128 * CTAS)) over its efficiency.
+int choose_mx_config(int M, int N, const int* resident_ctas) {
     int best = 0;
     double best_cost = 0.0;
     for (int c = 0; c < kNumMxConfigs; ++c) {
         const KernelConfig& k = kMxConfigs[c];
         const long long tiles = static_cast<long long>((M + k.bm - 1) / k.bm) * ((N + k.bn - 1) / k.bn);
-        const long long waves = (tiles + num_sms - 1) / num_sms;
-        const double cost = static_cast<double>(waves) * (k.bn / 128.0) / k.eff;
-        if (c == 0 || cost < best_cost) {
+        const long long slots = resident_ctas[c] / k.ctas;
+        if (slots < 1) continue;
+        const long long waves = (tiles + slots - 1) / slots;
+        const double cost = static_cast<double>(waves) * (k.bm * k.bn / (128.0 * 128.0 * k.ctas)) / k.eff;
+        if (best_cost == 0.0 || cost < best_cost) {
             best = c;
             best_cost = cost;
         }
@@ -158,18 +163,14 @@ int device_setup(int dev) {
             st.status = HGEMM_ERR_CUDA;
             return;
         }
-        static_assert(kNumConfigs <= kMaxConfigs, "raise kMaxConfigs");
-        for (int c = 1; c < kNumConfigs; ++c) {
-            const KernelConfig& k = kConfigs[c];
+        static_assert(kNumConfigs <= kMaxConfigs && kNumMxConfigs <= kMaxConfigs, "raise kMaxConfigs");
+        // Shared memory opt-in, then the CTAs that can be resident at once (0 on failure).
+        auto resident = [&](const KernelConfig& k) -> int {
             if (cudaFuncSetAttribute(k.kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, k.smem_bytes) !=
                 cudaSuccess) {
-                st.status = HGEMM_ERR_CUDA;
-                return;
+                return 0;
             }
-            if (k.ctas == 1) {
-                st.resident_ctas[c] = prop.multiProcessorCount;
-                continue;
-            }
+            if (k.ctas == 1) return prop.multiProcessorCount;
             cudaLaunchConfig_t cfg{};
             cudaLaunchAttribute attr[1];
             attr[0].id = cudaLaunchAttributeClusterDimension;
@@ -184,14 +185,20 @@ int device_setup(int dev) {
             int clusters = 0;
             if (cudaOccupancyMaxActiveClusters(&clusters, k.kernel, &cfg) != cudaSuccess || clusters <= 0) {
                 cudaGetLastError();
+                return 0;
+            }
+            return clusters * k.ctas;
+        };
+        for (int c = 1; c < kNumConfigs; ++c) {
+            st.resident_ctas[c] = resident(kConfigs[c]);
+            if (st.resident_ctas[c] == 0) {
                 st.status = HGEMM_ERR_CUDA;
                 return;
             }
-            st.resident_ctas[c] = clusters * k.ctas;
         }
-        for (const KernelConfig& k : kMxConfigs) {
-            if (cudaFuncSetAttribute(k.kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, k.smem_bytes) !=
-                cudaSuccess) {
+        for (int c = 0; c < kNumMxConfigs; ++c) {
+            st.mx_resident_ctas[c] = resident(kMxConfigs[c]);
+            if (st.mx_resident_ctas[c] == 0) {
                 st.status = HGEMM_ERR_CUDA;
                 return;
             }
@@ -234,6 +241,19 @@ bool encode_2d(CUtensorMap* map, CUtensorMapDataType dtype, size_t elem_bytes, c
     const cuuint32_t estr[2] = {1, 1};
     return g_encode(map, dtype, 2, const_cast<void*>(ptr), dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
                     swizzle, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                    CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
+
+// An MX scale-factor tensor in the blocked layout as a 3-D map: x = 128 bytes, y = k_rows
+// 128-byte rows along K (4 per atom), z = row_blocks 128-row blocks; box 128 x 4 x
+// box_blocks (one K block's atoms).  Out-of-range blocks read as zeros.
+bool encode_sf_3d(CUtensorMap* map, const void* ptr, uint64_t k_rows, uint64_t row_blocks, uint32_t box_blocks) {
+    const cuuint64_t dims[3] = {128, k_rows, row_blocks};
+    const cuuint64_t strides[2] = {128, k_rows * 128};
+    const cuuint32_t box[3] = {128, static_cast<cuuint32_t>(kSfRowsPerAtom), box_blocks};
+    const cuuint32_t estr[3] = {1, 1, 1};
+    return g_encode(map, CU_TENSOR_MAP_DATA_TYPE_UINT8, 3, const_cast<void*>(ptr), dims, strides, box, estr,
+                    CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
                     CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
 }
 
@@ -395,7 +415,8 @@ int run_gemm(const void* A, const void* B, void* C, int M, int N, int K, const f
     p.dp_tiles = sc.dp_tiles;
     p.sk_tiles = sc.sk_tiles;
     p.sk_slots = sc.sk_slots;
-    if (sc.sk_tiles == 0) return kc.launch(ta, tb, tc, p, peers, sc.grid, stream);
+    const SfMaps no_sf{};
+    if (sc.sk_tiles == 0) return kc.launch(ta, tb, tc, p, peers, no_sf, sc.grid, stream);
 
     const size_t need = sc.partial_bytes + sc.counter_bytes;
     void* ws = workspace;
@@ -408,7 +429,7 @@ int run_gemm(const void* A, const void* B, void* C, int M, int N, int K, const f
     p.partials = static_cast<float*>(ws);
     p.counters = reinterpret_cast<int*>(static_cast<uint8_t*>(ws) + sc.partial_bytes);
     rc = cudaMemsetAsync(p.counters, 0, sc.counter_bytes, stream) == cudaSuccess ? HGEMM_OK : HGEMM_ERR_CUDA;
-    if (rc == HGEMM_OK) rc = kc.launch(ta, tb, tc, p, peers, sc.grid, stream);
+    if (rc == HGEMM_OK) rc = kc.launch(ta, tb, tc, p, peers, no_sf, sc.grid, stream);
     if (!workspace && cudaFreeAsync(ws, stream) != cudaSuccess && rc == HGEMM_OK) rc = HGEMM_ERR_CUDA;
     return rc;
 }
@@ -427,7 +448,8 @@ int run_gemm_mx(const void* A, const void* B, void* C, int M, int N, int K, cons
         return cudaMemsetAsync(C, 0, static_cast<size_t>(M) * N * 2, stream) == cudaSuccess ? HGEMM_OK
                                                                                               : HGEMM_ERR_CUDA;
     }
-    const KernelConfig& kc = kMxConfigs[config > 0 ? config - 1 : choose_mx_config(M, N, dev->num_sms)];
+    const int ci = config > 0 ? config - 1 : choose_mx_config(M, N, dev->mx_resident_ctas);
+    const KernelConfig& kc = kMxConfigs[ci];
     CUtensorMap ta, tb, tc;
     if (!encode_2d(&ta, CU_TENSOR_MAP_DATA_TYPE_UINT8, 1, A, static_cast<uint64_t>(K), static_cast<uint64_t>(M), 128,
                    128) ||
@@ -449,12 +471,20 @@ int run_gemm_mx(const void* A, const void* B, void* C, int M, int N, int K, cons
     p.scale_a = sa;
     p.scale_b = sb;
     p.dp_tiles = p.num_m_blocks * p.num_n_blocks;
-    p.sfa = static_cast<const uint8_t*>(sfa);
-    p.sfb = static_cast<const uint8_t*>(sfb);
     p.sf_k_atoms = (K + 127) / 128;
+    // Scale factors as (128 bytes, 4 rows per atom along K, 128-row blocks); boxes of one
+    // atom along K by 1 (A) or BN / 128 (B) row blocks, no swizzle.
+    SfMaps sfm{};
+    const uint64_t k_rows = static_cast<uint64_t>(p.sf_k_atoms) * kSfRowsPerAtom;
+    if (!encode_sf_3d(&sfm.a, sfa, k_rows, static_cast<uint64_t>((M + 127) / 128), 1) ||
+        !encode_sf_3d(&sfm.b, sfb, k_rows, static_cast<uint64_t>((N + 127) / 128),
+                      static_cast<uint32_t>(kc.bn / 128))) {
+        return HGEMM_ERR_CUDA;
+    }
     const PeerOutputs peers{};
-    const int grid = std::min(p.dp_tiles, dev->num_sms);
-    return kc.launch(ta, tb, tc, p, peers, grid, stream);
+    const int slots = dev->mx_resident_ctas[ci] / kc.ctas;
+    const int grid = kc.ctas * std::min(p.dp_tiles, slots);
+    return kc.launch(ta, tb, tc, p, peers, sfm, grid, stream);
 }
 
 }  // namespace

@@ -170,6 +170,25 @@ __device__ __forceinline__ void tma_load_2d_hint(uint32_t smem_dst, const void* 
 
 // CTA-pair form (cta_group::2): the data lands in this CTA's shared memory and the
 // transaction bytes complete `cluster_bar`, which may be the peer CTA's barrier.
+// 3-D tiled loads (the MX scale-factor boxes), own-barrier and pair forms.
+__device__ __forceinline__ void tma_load_3d(uint32_t smem_dst, const void* tmap, int32_t x, int32_t y, int32_t z,
+                                            uint32_t bar) {
+    asm volatile(
+        "cp.async.bulk.tensor.3d.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3, %4}], "
+        "[%5];" ::"r"(smem_dst),
+        "l"(reinterpret_cast<uint64_t>(tmap)), "r"(x), "r"(y), "r"(z), "r"(bar)
+        : "memory");
+}
+
+__device__ __forceinline__ void tma_load_3d_pair(uint32_t smem_dst, const void* tmap, int32_t x, int32_t y,
+                                                 int32_t z, uint32_t cluster_bar) {
+    asm volatile(
+        "cp.async.bulk.tensor.3d.cta_group::2.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%2, "
+        "%3, %4}], [%5];" ::"r"(smem_dst),
+        "l"(reinterpret_cast<uint64_t>(tmap)), "r"(x), "r"(y), "r"(z), "r"(cluster_bar)
+        : "memory");
+}
+
 __device__ __forceinline__ void tma_load_2d_pair(uint32_t smem_dst, const void* tmap, int32_t x, int32_t y,
                                                  uint32_t cluster_bar) {
     asm volatile(
@@ -349,20 +368,17 @@ __host__ __device__ constexpr uint32_t idesc_e4m3_f32(int m, int n) {
 
 // ---- MX block scaling (kind::mxf8f6f4.block_scale) ---------------------------------------
 
-// 1-D bulk copy global -> this CTA's shared memory (16-byte aligned, size % 16 == 0),
-// completing `bar`.
-__device__ __forceinline__ void bulk_load_1d(uint32_t smem_dst, const void* src, uint32_t bytes, uint32_t bar) {
-    asm volatile("cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(
-                     smem_dst),
-                 "l"(reinterpret_cast<uint64_t>(src)), "r"(bytes), "r"(bar)
-                 : "memory");
-}
-
 // Shared -> tensor memory: 32 rows x 128 bits, written to lanes [0, 32) of all four lane
-// quadrants (columns taddr .. taddr + 3).  Issued by one thread; ordered with the
-// thread's later tcgen05.mma.
+// quadrants (columns taddr .. taddr + 3).  Issued by one thread; executes in order with the
+// thread's tcgen05.mma.  For a CTA pair (cta_group::2) each CTA's tensor memory is filled
+// from its own shared memory at the same address.
+template <int CTAS>
 __device__ __forceinline__ void tmem_cp_32x128b_warpx4(uint32_t taddr, uint64_t src_desc) {
-    asm volatile("tcgen05.cp.cta_group::1.32x128b.warpx4 [%0], %1;" ::"r"(taddr), "l"(src_desc) : "memory");
+    if constexpr (CTAS == 2) {
+        asm volatile("tcgen05.cp.cta_group::2.32x128b.warpx4 [%0], %1;" ::"r"(taddr), "l"(src_desc) : "memory");
+    } else {
+        asm volatile("tcgen05.cp.cta_group::1.32x128b.warpx4 [%0], %1;" ::"r"(taddr), "l"(src_desc) : "memory");
+    }
 }
 
 // Descriptor of a 32 x 16-byte scale-factor block in shared memory: no swizzle, K-major,
@@ -385,14 +401,26 @@ __host__ __device__ constexpr uint32_t idesc_mx_e4m3(int m, int n, uint32_t sf_i
            (sf_id << 29);
 }
 
+template <int CTAS>
 __device__ __forceinline__ void mma_mxf8f6f4(uint32_t d_tmem, uint64_t a_desc, uint64_t b_desc, uint32_t idesc,
                                              uint32_t tsfa, uint32_t tsfb, uint32_t accumulate) {
-    asm volatile(
-        "{\n\t.reg .pred p;\n\t"
-        "setp.ne.b32 p, %4, 0;\n\t"
-        "tcgen05.mma.cta_group::1.kind::mxf8f6f4.block_scale [%0], %1, %2, %3, [%5], [%6], p;\n\t}\n" ::"r"(d_tmem),
-        "l"(a_desc), "l"(b_desc), "r"(idesc), "r"(accumulate), "r"(tsfa), "r"(tsfb)
-        : "memory");
+    if constexpr (CTAS == 2) {
+        asm volatile(
+            "{\n\t.reg .pred p;\n\t"
+            "setp.ne.b32 p, %4, 0;\n\t"
+            "tcgen05.mma.cta_group::2.kind::mxf8f6f4.block_scale [%0], %1, %2, %3, [%5], [%6], p;\n\t}\n" ::"r"(
+                d_tmem),
+            "l"(a_desc), "l"(b_desc), "r"(idesc), "r"(accumulate), "r"(tsfa), "r"(tsfb)
+            : "memory");
+    } else {
+        asm volatile(
+            "{\n\t.reg .pred p;\n\t"
+            "setp.ne.b32 p, %4, 0;\n\t"
+            "tcgen05.mma.cta_group::1.kind::mxf8f6f4.block_scale [%0], %1, %2, %3, [%5], [%6], p;\n\t}\n" ::"r"(
+                d_tmem),
+            "l"(a_desc), "l"(b_desc), "r"(idesc), "r"(accumulate), "r"(tsfa), "r"(tsfb)
+            : "memory");
+    }
 }
 
 // ---- conversions -------------------------------------------------------------------------

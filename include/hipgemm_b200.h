@@ -186,7 +186,8 @@ const char* hgemm_version(void);
 int hgemm_fp8_tn_mx(const void* A, const void* B, void* C, int M, int N, int K, const void* SFA, const void* SFB,
                     const float* d_scale_a, const float* d_scale_b, hgemm_stream_t stream);
 /* hgemm_fp8_tn_mx with its kernel chosen: 0 = by wave count (what hgemm_fp8_tn_mx does),
- * 1 = 128 x 256 tiles, one accumulator; 2 = 128 x 128 tiles.  Names: hgemm_mx_config_name. */
+ * 1 = 128 x 256 tiles, one accumulator; 2 = 128 x 128 tiles; 3 = 256 x 256 tiles on CTA
+ * pairs, one accumulator.  Names: hgemm_mx_config_name. */
 int hgemm_fp8_tn_mx_config(const void* A, const void* B, void* C, int M, int N, int K, const void* SFA,
                            const void* SFB, const float* d_scale_a, const float* d_scale_b, int config,
                            hgemm_stream_t stream);

@@ -43,7 +43,7 @@ def _mx_operand(rows, K, seed):
     return oracle.quantize_mx(x)
 
 
-@pytest.mark.parametrize("config", [1, 2])
+@pytest.mark.parametrize("config", [1, 2, 3])
 @pytest.mark.parametrize("M,N,K", [(128, 128, 128), (256, 384, 1024), (300, 520, 1056), (1000, 1032, 2080),
                                    (4096, 4096, 4096)])
 def test_mx_gemm_matches_oracle(cuda_device, M, N, K, config):
@@ -82,7 +82,7 @@ def test_mx_unit_scales_equal_plain_gemm(cuda_device):
     plain = hg.fp8_gemm_tn(a, b)
     ref = oracle.gemm(A, B)
     assert oracle.validate(c_bits(plain), ref)[0] == 0
-    for config in (0, 1, 2):
+    for config in (0, 1, 2, 3):
         mx = hg.fp8_gemm_tn_mx(a, b, ones_a, ones_b, config=config)
         assert oracle.validate(c_bits(mx), ref)[0] == 0, config
 
@@ -97,7 +97,7 @@ def test_mx_repeated_calls_identical(cuda_device):
     a, b = torch.from_numpy(A).cuda(), torch.from_numpy(B).cuda()
     sfa = hg.mx_sf_to_blocked(torch.from_numpy(SFA), K).cuda()
     sfb = hg.mx_sf_to_blocked(torch.from_numpy(SFB), K).cuda()
-    for config in (1, 2):
+    for config in (1, 2, 3):
         first = hg.fp8_gemm_tn_mx(a, b, sfa, sfb, config=config)
         for _ in range(3):
             assert torch.equal(hg.fp8_gemm_tn_mx(a, b, sfa, sfb, config=config).view(torch.int16),

@@ -111,7 +111,7 @@ constexpr int kNumConfigs = sizeof(kConfigs) / sizeof(kConfigs[0]);
 // 128 x 128 tiles with two for grids too small to fill the GPU with the wide tiles.  eff:
 // measured per-SM throughput at 8192^3 relative to the best config.
 const KernelConfig kMxConfigs[] = {
-    make_config<1, 256, 4, true>("mx_bn256_s4", 0.90),
+    make_config<1, 256, 4, true>("mx_bn256_s4", 0.95),
     make_config<1, 128, 5, true>("mx_bn128_s5", 0.52),
     make_config<2, 256, 6, true>("mx_pair256_s6", 1.0),
 };

@@ -11,11 +11,11 @@ from ._lib import (HGEMM_ERR_ALIGNMENT, HGEMM_ERR_CUDA, HGEMM_ERR_DEVICE_TIMEOUT
                    lib)
 from .gemm import (device_status, fp8_gemm_tn, fp8_gemm_tn_from_host, fp8_gemm_tn_mx, fp8_gemm_tn_rows,
                    host_init_random, host_make_quantized, mx_sf_to_blocked, plan, quantize_e4m3,
-                   quantize_mx_e4m3)
+                   quantize_e4m3_delayed, quantize_mx_e4m3)
 
 __all__ = [
     "HGEMM_OK", "HGEMM_ERR_INVALID_VALUE", "HGEMM_ERR_ALIGNMENT", "HGEMM_ERR_UNSUPPORTED", "HGEMM_ERR_CUDA",
     "HGEMM_ERR_NO_DEVICE", "HGEMM_ERR_DEVICE_TIMEOUT", "HGEMM_SCHEDULE_AUTO", "HGEMM_SCHEDULE_DATA_PARALLEL",
     "HGEMM_SCHEDULE_STREAM_K", "LIB_PATH", "HgemmError", "check", "config_names", "lib",
-    "device_status", "fp8_gemm_tn", "fp8_gemm_tn_from_host", "fp8_gemm_tn_mx", "fp8_gemm_tn_rows", "mx_sf_to_blocked", "quantize_mx_e4m3", "host_init_random", "host_make_quantized", "plan", "quantize_e4m3",
+    "device_status", "fp8_gemm_tn", "fp8_gemm_tn_from_host", "fp8_gemm_tn_mx", "fp8_gemm_tn_rows", "mx_sf_to_blocked", "quantize_mx_e4m3", "quantize_e4m3_delayed", "host_init_random", "host_make_quantized", "plan", "quantize_e4m3",
 ]

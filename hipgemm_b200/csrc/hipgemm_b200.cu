@@ -519,10 +519,9 @@ size_t hgemm_mx_sf_bytes(int rows, int K) {
 
 int hgemm_host_mx_sf_to_blocked(const uint8_t* sf, int rows, int K, uint8_t* blocked) {
     if (rows < 0 || K < 0 || K % 32 != 0 || (rows > 0 && K > 0 && (!sf || !blocked))) return HGEMM_ERR_INVALID_VALUE;
-    const int groups = K / 32, k_atoms = (K + 127) / 128, row_atoms = (rows + 127) / 128;
+    const int groups = K / 32, k_atoms = (K + 127) / 128;
     // Padding (rows past `rows`, groups past K/32) holds 127 = 2^0, a finite scale.
     std::memset(blocked, 127, hgemm_mx_sf_bytes(rows, K));
-    (void)row_atoms;
     for (int r = 0; r < rows; ++r) {
         for (int g = 0; g < groups; ++g) {
             const size_t atom = static_cast<size_t>(r / 128) * k_atoms + g / 4;
@@ -532,7 +531,6 @@ int hgemm_host_mx_sf_to_blocked(const uint8_t* sf, int rows, int K, uint8_t* blo
     }
     return HGEMM_OK;
 }
-
 
 int hgemm_fp8_tn(const void* A, const void* B, void* C, int M, int N, int K, const float* d_scale_a,
                  const float* d_scale_b, hgemm_stream_t stream) {

@@ -120,6 +120,56 @@ __global__ void __launch_bounds__(kThreads) quantize_kernel(const T* __restrict_
     }
 }
 
+// Delayed scaling in one pass: q = e4m3(x / scale_in) with a scale the caller carries over
+// (from the previous step's amax, as FP8 training and serving loops do), and amax(|x|) of
+// this tensor accumulated into *amax_bits for the next step.  16 elements per thread and
+// step, one atomicMax per block.
+template <typename T>
+__global__ void __launch_bounds__(kThreads) quantize_delayed_kernel(const T* __restrict__ x, size_t n,
+                                                                     const float* __restrict__ scale_in,
+                                                                     uint8_t* __restrict__ q,
+                                                                     unsigned int* __restrict__ amax_bits) {
+    constexpr int E = Vec<T>::kElems;
+    constexpr int LOADS = 16 / E;
+    const float s = *scale_in;
+    const size_t ngroups = n / 16;
+    const size_t stride = static_cast<size_t>(gridDim.x) * blockDim.x;
+    float m = 0.0f;
+    for (size_t g = static_cast<size_t>(blockIdx.x) * blockDim.x + threadIdx.x; g < ngroups; g += stride) {
+        float f[16];
+#pragma unroll
+        for (int l = 0; l < LOADS; ++l) {
+            float v[E];
+            Vec<T>::load(x, g * LOADS + l, v);
+#pragma unroll
+            for (int i = 0; i < E; ++i) {
+                m = fmaxf(m, fabsf(v[i]));
+                f[l * E + i] = __fdiv_rn(v[i], s);
+            }
+        }
+        uint32_t w[4];
+#pragma unroll
+        for (int i = 0; i < 4; ++i) w[i] = e4m3x2(f[4 * i], f[4 * i + 1]) | (e4m3x2(f[4 * i + 2], f[4 * i + 3]) << 16);
+        reinterpret_cast<uint4*>(q)[g] = make_uint4(w[0], w[1], w[2], w[3]);
+    }
+    for (size_t i = ngroups * 16 + static_cast<size_t>(blockIdx.x) * blockDim.x + threadIdx.x; i < n; i += stride) {
+        const float v = load_as_float(x, i);
+        m = fmaxf(m, fabsf(v));
+        q[i] = static_cast<uint8_t>(e4m3x2(__fdiv_rn(v, s), 0.0f) & 0xFFu);
+    }
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
+    __shared__ float warp_max[kThreads / 32];
+    if ((threadIdx.x & 31) == 0) warp_max[threadIdx.x / 32] = m;
+    __syncthreads();
+    if (threadIdx.x < 32) {
+        m = threadIdx.x < kThreads / 32 ? warp_max[threadIdx.x] : 0.0f;
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
+        if (threadIdx.x == 0) atomicMax(amax_bits, __float_as_uint(m));
+    }
+}
+
 // Turns the accumulated amax bits into the scale, in place.
 __global__ void finalize_scale_kernel(unsigned int* amax_bits) {
     const float s = scale_from_amax(*amax_bits);
@@ -283,7 +333,32 @@ int run_mx(const T* x, int rows, int K, uint8_t* q, uint8_t* sf, cudaStream_t st
     return cudaGetLastError() == cudaSuccess ? HGEMM_OK : HGEMM_ERR_CUDA;
 }
 
+template <typename T>
+int run_delayed(const T* x, size_t n, const float* scale_in, uint8_t* q, float* amax_out, cudaStream_t stream) {
+    unsigned int* acc = reinterpret_cast<unsigned int*>(amax_out);
+    if (cudaMemsetAsync(acc, 0, sizeof(unsigned int), stream) != cudaSuccess) return HGEMM_ERR_CUDA;
+    if (n > 0) {
+        quantize_delayed_kernel<T><<<grid_for(quantize_delayed_kernel<T>, n / 16 + 1), kThreads, 0, stream>>>(
+            x, n, scale_in, q, acc);
+    }
+    return cudaGetLastError() == cudaSuccess ? HGEMM_OK : HGEMM_ERR_CUDA;
+}
+
 }  // namespace hgq
+
+extern "C" int hgemm_quantize_e4m3_delayed(const void* x, int x_dtype, size_t n, void* q, const float* d_scale_in,
+                                           float* d_amax_out, hgemm_stream_t stream) {
+    if (!d_scale_in || !d_amax_out || (n > 0 && (!x || !q))) return HGEMM_ERR_INVALID_VALUE;
+    if (x_dtype != HGEMM_DTYPE_F32 && x_dtype != HGEMM_DTYPE_BF16) return HGEMM_ERR_INVALID_VALUE;
+    if ((reinterpret_cast<uintptr_t>(x) & 15u) || (reinterpret_cast<uintptr_t>(q) & 15u) ||
+        (reinterpret_cast<uintptr_t>(d_scale_in) & 3u) || (reinterpret_cast<uintptr_t>(d_amax_out) & 3u)) {
+        return HGEMM_ERR_ALIGNMENT;
+    }
+    const cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
+    uint8_t* const out = static_cast<uint8_t*>(q);
+    if (x_dtype == HGEMM_DTYPE_F32) return hgq::run_delayed(static_cast<const float*>(x), n, d_scale_in, out, d_amax_out, s);
+    return hgq::run_delayed(static_cast<const __nv_bfloat16*>(x), n, d_scale_in, out, d_amax_out, s);
+}
 
 extern "C" int hgemm_quantize_mx_e4m3(const void* x, int x_dtype, int rows, int K, void* q, void* sf_blocked,
                                       hgemm_stream_t stream) {

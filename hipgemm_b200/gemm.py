@@ -161,6 +161,36 @@ def quantize_e4m3(x: torch.Tensor, out: torch.Tensor | None = None, scale: torch
     return out, scale
 
 
+def quantize_e4m3_delayed(x: torch.Tensor, scale_in: torch.Tensor, out: torch.Tensor | None = None,
+                          amax_out: torch.Tensor | None = None,
+                          stream: torch.cuda.Stream | None = None) -> tuple[torch.Tensor, torch.Tensor]:
+    """Delayed-scaling e4m3 quantisation in one pass (hgemm_quantize_e4m3_delayed): returns
+    (q, amax) with q = e4m3(x / scale_in) and amax = max|x| of this x (1-element float32), from
+    which the caller forms the next scale (e.g. amax / 448)."""
+    if not x.is_cuda or not x.is_contiguous():
+        raise ValueError("x must be a contiguous CUDA tensor (there is no CPU path)")
+    if x.dtype == torch.float32:
+        dt = 0
+    elif x.dtype == torch.bfloat16:
+        dt = 1
+    else:
+        raise TypeError(f"x must be float32 or bfloat16, got {x.dtype}")
+    _check_scale("scale_in", scale_in, x.device)
+    if scale_in is None:
+        raise ValueError("scale_in is required")
+    if out is None:
+        out = torch.empty(x.shape, dtype=torch.uint8, device=x.device)
+    if amax_out is None:
+        amax_out = torch.empty(1, dtype=torch.float32, device=x.device)
+    if out.numel() != x.numel() or out.dtype != torch.uint8 or not out.is_contiguous():
+        raise ValueError("out must be a contiguous uint8 tensor with x's size")
+    with torch.cuda.device(x.device):
+        rc = lib().hgemm_quantize_e4m3_delayed(x.data_ptr(), dt, x.numel(), out.data_ptr(), scale_in.data_ptr(),
+                                               amax_out.data_ptr(), _stream_handle(stream))
+    check(rc, "hgemm_quantize_e4m3_delayed")
+    return out, amax_out
+
+
 def fp8_gemm_tn_from_host(a_host: torch.Tensor, b_host: torch.Tensor, c_host: torch.Tensor,
                           scales_host: torch.Tensor | None, d_a: torch.Tensor, d_b: torch.Tensor, d_c: torch.Tensor,
                           d_scales: torch.Tensor | None = None, stream: torch.cuda.Stream | None = None) -> torch.Tensor:

@@ -213,6 +213,14 @@ int hgemm_host_mx_sf_to_blocked(const uint8_t* sf, int rows, int K, uint8_t* blo
  * quantiser moved onto the GPU. */
 int hgemm_quantize_e4m3(const void* x, int x_dtype, size_t n, void* q, float* d_scale, hgemm_stream_t stream);
 
+/* Delayed scaling, one HBM pass: q = e4m3(x / *d_scale_in) (IEEE division, satfinite RNE; the
+ * scale is used as given, typically amax/448 of the previous step), and *d_amax_out =
+ * amax(|x|) of this tensor (NaNs ignored) for the next step's scale.  With *d_scale_in equal
+ * to this tensor's own amax/448 the bytes equal hgemm_quantize_e4m3's.  x and q 16-byte
+ * aligned, the two floats 4-byte aligned, all on the device.  Stream-ordered, no sync. */
+int hgemm_quantize_e4m3_delayed(const void* x, int x_dtype, size_t n, void* q, const float* d_scale_in,
+                                float* d_amax_out, hgemm_stream_t stream);
+
 /* OCP MX e4m3 quantiser on the device: x (rows x K, fp32 or bf16 by x_dtype, row-major) ->
  * q (rows x K e4m3 bytes) and one e8m0 scale per 32 elements of a row, written in the
  * blocked layout hgemm_fp8_tn_mx reads (hgemm_mx_sf_bytes(rows, K) bytes; padding = 127).

@@ -31,6 +31,7 @@ _SIG = {
     "oracle_normal_f32": (None, [_vp, ctypes.c_size_t, ctypes.c_uint64, _f, _f]),
     "oracle_init_random_fp8": (None, [_vp, ctypes.c_size_t, ctypes.c_uint64, _f, _f]),
     "oracle_quantize_e4m3": (_f, [_vp, ctypes.c_size_t, _vp]),
+    "oracle_quantize_e4m3_with_scale": (_f, [_vp, ctypes.c_size_t, _f, _vp]),
     "oracle_make_quantized": (_f, [_vp, ctypes.c_size_t, ctypes.c_uint64, _f, _f]),
     "oracle_gemm_rows": (None, [_vp, _vp, _vp, _i, _i, _i, _f, _f, _i, _i, _i]),
     "oracle_gemm_naive_rows": (None, [_vp, _vp, _vp, _i, _i, _i, _f, _f, _i, _i, _i]),
@@ -124,6 +125,14 @@ def quantize(x: np.ndarray) -> tuple[np.ndarray, float]:
     q = np.empty(x.shape, dtype=np.uint8)
     s = lib().oracle_quantize_e4m3(_p(x), x.size, _p(q))
     return q, float(s)
+
+
+def quantize_with_scale(x: np.ndarray, scale: float) -> tuple[np.ndarray, float]:
+    """Delayed scaling: (e4m3(x / scale), amax|x|)."""
+    x = np.ascontiguousarray(x, dtype=np.float32)
+    q = np.empty(x.shape, dtype=np.uint8)
+    amax = lib().oracle_quantize_e4m3_with_scale(_p(x), x.size, float(scale), _p(q))
+    return q, float(amax)
 
 
 def make_quantized(shape: tuple[int, int], seed: int, mean: float = 0.0, stddev: float = 1.0) -> tuple[np.ndarray, float]:

@@ -182,6 +182,15 @@ float oracle_quantize_e4m3(const float* x, size_t n, uint8_t* q) {
     return scale;
 }
 
+float oracle_quantize_e4m3_with_scale(const float* x, size_t n, float scale, uint8_t* q) {
+    float amax = 0.0f;
+    for (size_t i = 0; i < n; ++i) {
+        amax = std::max(amax, std::fabs(x[i]));
+        q[i] = encode_e4m3(x[i] / scale);
+    }
+    return amax;
+}
+
 float oracle_make_quantized(uint8_t* q, size_t n, uint64_t seed, float mean, float stddev) {
     std::vector<float> x(n);
     oracle_normal_f32(x.data(), n, seed, mean, stddev);

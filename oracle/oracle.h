@@ -56,6 +56,8 @@ void oracle_init_random_fp8(uint8_t* out, size_t n, uint64_t seed, float mean, f
 /* Per-tensor quantiser of the benchmark configs: scale = amax/448 (fp32),
  * q = e4m3(x / scale).  Returns the scale; an all-zero tensor gets scale 1. */
 float oracle_quantize_e4m3(const float* x, size_t n, uint8_t* q);
+/* Delayed scaling: q = e4m3(x / scale) with the scale given; returns amax(|x|) (NaNs ignored). */
+float oracle_quantize_e4m3_with_scale(const float* x, size_t n, float scale, uint8_t* q);
 /* Draw + quantise in one pass: N(mean, stddev) from mt19937(seed), then
  * oracle_quantize_e4m3.  Returns the scale. */
 float oracle_make_quantized(uint8_t* q, size_t n, uint64_t seed, float mean, float stddev);

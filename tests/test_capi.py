@@ -176,3 +176,16 @@ def test_mx_quantiser_argument_checks():
     assert q(FAKE + 8, 1, 4, 64, FAKE, FAKE, None) == hg.HGEMM_ERR_ALIGNMENT
     assert q(FAKE, 0, 4, 64, FAKE + 4, FAKE, None) == hg.HGEMM_ERR_ALIGNMENT
     assert q(None, 0, 0, 64, None, None, None) == hg.HGEMM_OK                    # nothing to do
+
+
+def test_delayed_quantiser_argument_checks():
+    L = hg.lib()
+    f = L.hgemm_quantize_e4m3_delayed
+    assert f(FAKE, 0, 16, FAKE, None, FAKE, None) == hg.HGEMM_ERR_INVALID_VALUE   # no scale_in
+    assert f(FAKE, 0, 16, FAKE, FAKE, None, None) == hg.HGEMM_ERR_INVALID_VALUE   # no amax_out
+    assert f(None, 0, 16, FAKE, FAKE, FAKE, None) == hg.HGEMM_ERR_INVALID_VALUE
+    assert f(FAKE, 3, 16, FAKE, FAKE, FAKE, None) == hg.HGEMM_ERR_INVALID_VALUE   # dtype
+    assert f(FAKE + 4, 0, 16, FAKE, FAKE, FAKE, None) == hg.HGEMM_ERR_ALIGNMENT
+    assert f(FAKE, 1, 16, FAKE + 8, FAKE, FAKE, None) == hg.HGEMM_ERR_ALIGNMENT
+    assert f(FAKE, 0, 16, FAKE, FAKE + 2, FAKE, None) == hg.HGEMM_ERR_ALIGNMENT
+    assert f(FAKE, 0, 16, FAKE, FAKE, FAKE + 1, None) == hg.HGEMM_ERR_ALIGNMENT

@@ -255,3 +255,16 @@ def test_mx_blocked_scale_layout(rows, K):
             rr = r % 128
             want[atom * 512 + 16 * (rr % 32) + 4 * (rr // 32) + g % 4] = sf[r, g]
     assert np.array_equal(got, want)
+
+
+def test_delayed_scaling_quantiser_known_answers():
+    x = np.array([1.0, -3.0, np.nan, 0.5, 500.0, -np.inf], dtype=np.float32)
+    q, amax = oracle.quantize_with_scale(x, 2.0)
+    assert q.tolist()[:5] == [0x30, 0xBC, 0x7F, 0x28, 0x78]  # 0.5, -1.5, NaN, 0.25, 250 -> 256
+    assert q[5] == 0xFE                                        # -inf / 2 saturates to -448
+    assert amax == float("inf")                                # NaN ignored, |-inf| counted
+    # With the tensor's own amax/448 the one-pass result is the two-pass quantiser's.
+    y = oracle.normal_f32(4099, 8, mean=0.5, stddev=3.0)
+    q2, s = oracle.quantize(y)
+    q1, a = oracle.quantize_with_scale(y, s)
+    assert np.array_equal(q1, q2) and np.float32(a) == np.float32(np.abs(y).max())

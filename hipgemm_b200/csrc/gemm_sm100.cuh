@@ -561,23 +561,38 @@ __global__ void __launch_bounds__(192, 1)
             const uint32_t tmem_row = tmem_base + ((quad * 32u) << 16) + static_cast<uint32_t>(acc * BN);
 
             if constexpr (S::EARLY_RELEASE) {
-                // The whole row into registers as bf16, then the accumulator is free for the
-                // next tile's MMAs while this one is stored (data-parallel tiles only).
-                uint32_t packed[BN / 2];
+                // Drain the row as bf16, then free the accumulator for the next tile's MMAs
+                // while this one is stored (data-parallel tiles only).  The first two chunks
+                // go straight to the warp's two staging buffers; the rest wait in registers.
+                constexpr int kDirect = 2;
+                constexpr int kHeld = BN / EC - kDirect;
+                uint32_t held[kHeld * (EC / 2)];
 #pragma unroll
-                for (int c = 0; c < BN / 16; ++c) {
-                    uint32_t r[16];
-                    tmem_ld_32x32b_x16(tmem_row + c * 16, r);
-                    tmem_ld_wait(r);
+                for (int c = 0; c < BN / EC; ++c) {
+                    uint32_t chunk[EC / 2];
 #pragma unroll
-                    for (int j = 0; j < 8; ++j) {
-                        packed[8 * c + j] = pack_bf16x2_rn(__fmul_rn(__uint_as_float(r[2 * j]), s),
-                                                           __fmul_rn(__uint_as_float(r[2 * j + 1]), s));
+                    for (int h = 0; h < EC / 16; ++h) {
+                        uint32_t r[16];
+                        tmem_ld_32x32b_x16(tmem_row + c * EC + h * 16, r);
+                        tmem_ld_wait(r);
+#pragma unroll
+                        for (int j = 0; j < 8; ++j) {
+                            chunk[8 * h + j] = pack_bf16x2_rn(__fmul_rn(__uint_as_float(r[2 * j]), s),
+                                                              __fmul_rn(__uint_as_float(r[2 * j + 1]), s));
+                        }
+                    }
+                    if (c < kDirect) {
+                        store_packed(chunk, row0, nb * BN + c * EC);
+                    } else {
+#pragma unroll
+                        for (int j = 0; j < EC / 2; ++j) held[(c - kDirect) * (EC / 2) + j] = chunk[j];
                     }
                 }
                 release_accumulator();
 #pragma unroll
-                for (int c = 0; c < BN / EC; ++c) store_packed(&packed[c * (EC / 2)], row0, nb * BN + c * EC);
+                for (int c = kDirect; c < BN / EC; ++c) {
+                    store_packed(&held[(c - kDirect) * (EC / 2)], row0, nb * BN + c * EC);
+                }
                 continue;
             }
             if (w.piece < 0) {

@@ -44,8 +44,8 @@ def _mx_operand(rows, K, seed):
 
 
 @pytest.mark.parametrize("config", [1, 2, 3])
-@pytest.mark.parametrize("M,N,K", [(128, 128, 128), (256, 384, 1024), (300, 520, 1056), (1000, 1032, 2080),
-                                   (4096, 4096, 4096)])
+@pytest.mark.parametrize("M,N,K", [(1, 8, 32), (129, 264, 160), (128, 128, 128), (256, 384, 1024), (300, 520, 1056),
+                                   (1000, 1032, 2080), (4096, 4096, 4096)])
 def test_mx_gemm_matches_oracle(cuda_device, M, N, K, config):
     import hipgemm_b200 as hg
     A, SFA = _mx_operand(M, K, M)

@@ -131,26 +131,37 @@ __global__ void __launch_bounds__(kThreads) quantize_delayed_kernel(const T* __r
                                                                      unsigned int* __restrict__ amax_bits) {
     constexpr int E = Vec<T>::kElems;
     constexpr int LOADS = 16 / E;
+    // Groups of 16 in flight per thread (all loads issued before any use): 2 for fp32, 1 for
+    // bf16 (measured at 8192 x 8192: fp32 60.8 -> 58.1 us with 2; bf16 49.3 -> 63.8 us).
+    constexpr int U = sizeof(T) == 4 ? 2 : 1;
     const float s = *scale_in;
     const size_t ngroups = n / 16;
     const size_t stride = static_cast<size_t>(gridDim.x) * blockDim.x;
     float m = 0.0f;
-    for (size_t g = static_cast<size_t>(blockIdx.x) * blockDim.x + threadIdx.x; g < ngroups; g += stride) {
-        float f[16];
+    for (size_t g0 = static_cast<size_t>(blockIdx.x) * blockDim.x + threadIdx.x; g0 < ngroups; g0 += U * stride) {
+        float v[U][16];
 #pragma unroll
-        for (int l = 0; l < LOADS; ++l) {
-            float v[E];
-            Vec<T>::load(x, g * LOADS + l, v);
+        for (int u = 0; u < U; ++u) {
+            const size_t g = g0 + u * stride;
+            if (g < ngroups) {
 #pragma unroll
-            for (int i = 0; i < E; ++i) {
-                m = fmaxf(m, fabsf(v[i]));
-                f[l * E + i] = __fdiv_rn(v[i], s);
+                for (int l = 0; l < LOADS; ++l) Vec<T>::load(x, g * LOADS + l, *reinterpret_cast<float(*)[E]>(&v[u][l * E]));
             }
         }
-        uint32_t w[4];
 #pragma unroll
-        for (int i = 0; i < 4; ++i) w[i] = e4m3x2(f[4 * i], f[4 * i + 1]) | (e4m3x2(f[4 * i + 2], f[4 * i + 3]) << 16);
-        reinterpret_cast<uint4*>(q)[g] = make_uint4(w[0], w[1], w[2], w[3]);
+        for (int u = 0; u < U; ++u) {
+            const size_t g = g0 + u * stride;
+            if (g >= ngroups) break;
+            uint32_t w[4];
+#pragma unroll
+            for (int i = 0; i < 16; ++i) m = fmaxf(m, fabsf(v[u][i]));
+#pragma unroll
+            for (int i = 0; i < 4; ++i) {
+                w[i] = e4m3x2(__fdiv_rn(v[u][4 * i], s), __fdiv_rn(v[u][4 * i + 1], s)) |
+                       (e4m3x2(__fdiv_rn(v[u][4 * i + 2], s), __fdiv_rn(v[u][4 * i + 3], s)) << 16);
+            }
+            reinterpret_cast<uint4*>(q)[g] = make_uint4(w[0], w[1], w[2], w[3]);
+        }
     }
     for (size_t i = ngroups * 16 + static_cast<size_t>(blockIdx.x) * blockDim.x + threadIdx.x; i < n; i += stride) {
         const float v = load_as_float(x, i);
@@ -338,7 +349,8 @@ int run_delayed(const T* x, size_t n, const float* scale_in, uint8_t* q, float* 
     unsigned int* acc = reinterpret_cast<unsigned int*>(amax_out);
     if (cudaMemsetAsync(acc, 0, sizeof(unsigned int), stream) != cudaSuccess) return HGEMM_ERR_CUDA;
     if (n > 0) {
-        quantize_delayed_kernel<T><<<grid_for(quantize_delayed_kernel<T>, n / 16 + 1), kThreads, 0, stream>>>(
+        quantize_delayed_kernel<T><<<grid_for(quantize_delayed_kernel<T>, n / (sizeof(T) == 4 ? 32 : 16) + 1), kThreads,
+                                     0, stream>>>(
             x, n, scale_in, q, acc);
     }
     return cudaGetLastError() == cudaSuccess ? HGEMM_OK : HGEMM_ERR_CUDA;

@@ -28,6 +28,15 @@
 //             MAC is a third lower than the 128 x 256 single-CTA tile; each CTA's tensor
 //             memory holds its 128 accumulator rows and each CTA runs its own epilogue.
 //
+// MX = true is the OCP MX variant: tcgen05.mma kind::mxf8f6f4.block_scale, with one e8m0
+// scale per 32 K elements of every row of A and B (the reference's MFMA builtin is this
+// instruction with its scales fixed at 2^0, fp8_4wave.hpp:53-58).  Each stage also carries
+// the K block's scale-factor atoms (two 3-D TMA boxes per CTA, on the operand barrier); the
+// MMA thread copies them into per-stage tensor-memory columns with tcgen05.cp before the
+// block's four MMAs.  For BN = 256 the scale factors take the columns a second accumulator
+// would use, so there is one accumulator and the epilogue releases it as soon as the tile is
+// drained (EARLY_RELEASE).
+//
 // CTA-pair synchronisation uses no multicast form: tcgen05.commit always targets a
 // barrier of the even CTA, and the even CTA forwards each completion to its peer with a
 // remote mbarrier.arrive that the peer acquires at cluster scope:

@@ -519,6 +519,7 @@ size_t hgemm_mx_sf_bytes(int rows, int K) {
 
 int hgemm_host_mx_sf_to_blocked(const uint8_t* sf, int rows, int K, uint8_t* blocked) {
     if (rows < 0 || K < 0 || K % 32 != 0 || (rows > 0 && K > 0 && (!sf || !blocked))) return HGEMM_ERR_INVALID_VALUE;
+    if (rows == 0 || K == 0) return HGEMM_OK;  // nothing to write
     const int groups = K / 32, k_atoms = (K + 127) / 128;
     // Padding (rows past `rows`, groups past K/32) holds 127 = 2^0, a finite scale.
     std::memset(blocked, 127, hgemm_mx_sf_bytes(rows, K));

@@ -163,6 +163,7 @@ def test_mx_argument_checks():
     assert L.hgemm_fp8_tn_mx(FAKE, FAKE, FAKE, 0, 8, 64, None, None, None, None, None) == hg.HGEMM_OK
     assert L.hgemm_mx_sf_bytes(300, 1056) == 3 * 9 * 512 and L.hgemm_mx_sf_bytes(0, 64) == 0
     assert L.hgemm_host_mx_sf_to_blocked(FAKE, 4, 48, FAKE) == hg.HGEMM_ERR_INVALID_VALUE
+    assert L.hgemm_host_mx_sf_to_blocked(None, 0, 64, None) == hg.HGEMM_OK  # empty: nothing touched
 
 
 def test_mx_quantiser_argument_checks():

@@ -49,3 +49,45 @@ def test_kernel_on_golden_fixture(cuda_device, path):
         c = hg.fp8_gemm_tn(a, b, sa, sb, config=config)
         got = c.view(torch.int16).cpu().numpy().view(np.uint16)
         assert oracle.validate(got, g["C"])[0] == 0, (path, config)
+
+
+def test_cuda_graph_capture_and_replay(cuda_device):
+    """After the first call on a device, the GEMM, the MX GEMM and the quantisers are plain
+    stream operations: a CUDA graph captures them, and replays on new input bytes give the
+    same bits as eager calls."""
+    import hipgemm_b200 as hg
+    M, N, K = 512, 768, 1024
+    g = torch.Generator(device="cuda").manual_seed(3)
+    xa = torch.randn(M, K, device="cuda", generator=g)
+    xb = torch.randn(N, K, device="cuda", generator=g)
+    # First calls on the device (one-time set-up happens outside the capture).
+    qa, sa = hg.quantize_e4m3(xa)
+    qb, sb = hg.quantize_e4m3(xb)
+    c = hg.fp8_gemm_tn(qa, qb, sa, sb)
+    ma, sfa = hg.quantize_mx_e4m3(xa)
+    mb, sfb = hg.quantize_mx_e4m3(xb)
+    cm = hg.fp8_gemm_tn_mx(ma, mb, sfa, sfb)
+    torch.cuda.synchronize()
+
+    stream = torch.cuda.Stream()
+    graph = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(graph, stream=stream):
+        hg.quantize_e4m3(xa, out=qa, scale=sa, stream=stream)
+        hg.quantize_e4m3(xb, out=qb, scale=sb, stream=stream)
+        hg.fp8_gemm_tn(qa, qb, sa, sb, out=c, stream=stream)
+        hg.quantize_mx_e4m3(xa, out=ma, sf_out=sfa, stream=stream)
+        hg.quantize_mx_e4m3(xb, out=mb, sf_out=sfb, stream=stream)
+        hg.fp8_gemm_tn_mx(ma, mb, sfa, sfb, out=cm, stream=stream)
+    for seed in (11, 12):
+        g.manual_seed(seed)
+        xa.copy_(torch.randn(M, K, device="cuda", generator=g))
+        xb.copy_(torch.randn(N, K, device="cuda", generator=g))
+        graph.replay()
+        torch.cuda.synchronize()
+        qa2, sa2 = hg.quantize_e4m3(xa)
+        qb2, sb2 = hg.quantize_e4m3(xb)
+        ma2, sfa2 = hg.quantize_mx_e4m3(xa)
+        mb2, sfb2 = hg.quantize_mx_e4m3(xb)
+        assert torch.equal(hg.fp8_gemm_tn(qa2, qb2, sa2, sb2).view(torch.int16), c.view(torch.int16))
+        assert torch.equal(hg.fp8_gemm_tn_mx(ma2, mb2, sfa2, sfb2).view(torch.int16), cm.view(torch.int16))
+    assert hg.device_status() == 0

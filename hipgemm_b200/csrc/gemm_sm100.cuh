@@ -338,6 +338,10 @@ __global__ void __launch_bounds__(192, 1)
     }
     tc_fence_after();
     const uint32_t tmem_base = *tmem_slot_ptr;
+    // Everything above (barriers, tensor memory, descriptor prefetch) may overlap the previous
+    // kernel's tail; global memory is read and written only after it has finished.
+    griddep_launch_dependents();
+    griddep_wait();
 
     const int slot = static_cast<int>(blockIdx.x) / CTAS;
     const int nslots = static_cast<int>(gridDim.x) / CTAS;

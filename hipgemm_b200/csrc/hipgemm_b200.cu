@@ -71,13 +71,22 @@ int launch_kernel(const CUtensorMap& ta, const CUtensorMap& tb, const CUtensorMa
     cfg.blockDim = dim3(S::kNumThreads, 1, 1);
     cfg.dynamicSmemBytes = static_cast<size_t>(S::SMEM_BYTES);
     cfg.stream = stream;
-    cudaLaunchAttribute attr[1];
-    attr[0].id = cudaLaunchAttributeClusterDimension;
-    attr[0].val.clusterDim.x = CTAS;
-    attr[0].val.clusterDim.y = 1;
-    attr[0].val.clusterDim.z = 1;
+    cudaLaunchAttribute attr[2];
+    unsigned n_attr = 0;
+    if (CTAS == 2) {
+        attr[n_attr].id = cudaLaunchAttributeClusterDimension;
+        attr[n_attr].val.clusterDim.x = CTAS;
+        attr[n_attr].val.clusterDim.y = 1;
+        attr[n_attr].val.clusterDim.z = 1;
+        ++n_attr;
+    }
+    // Programmatic dependent launch: the kernel may be scheduled while the stream's previous
+    // kernel (one of ours) finishes; it touches no global memory before griddepcontrol.wait.
+    attr[n_attr].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[n_attr].val.programmaticStreamSerializationAllowed = 1;
+    ++n_attr;
     cfg.attrs = attr;
-    cfg.numAttrs = CTAS == 2 ? 1 : 0;
+    cfg.numAttrs = n_attr;
     const cudaError_t e =
         cudaLaunchKernelEx(&cfg, fp8_gemm_tn_sm100<CTAS, BN, STAGES, MX>, ta, tb, tc, p, peers, sfm);
     return e == cudaSuccess ? HGEMM_OK : HGEMM_ERR_CUDA;

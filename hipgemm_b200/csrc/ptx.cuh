@@ -123,6 +123,15 @@ __device__ __forceinline__ void sleep_ns_bounded(uint64_t ns) {
     while (globaltimer_ns() - t0 < ns) __nanosleep(1000);
 }
 
+// ---- programmatic dependent launch ---------------------------------------------------------
+
+// Allow the stream's next kernel to be scheduled (it still waits in griddep_wait for this
+// grid to finish before touching memory).
+__device__ __forceinline__ void griddep_launch_dependents() { asm volatile("griddepcontrol.launch_dependents;" ::: "memory"); }
+// Wait until the previous kernel in the stream has completed and its memory is visible (no-op
+// when there is no programmatic dependency).
+__device__ __forceinline__ void griddep_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+
 // ---- cluster helpers -------------------------------------------------------------------
 
 __device__ __forceinline__ uint32_t cluster_ctarank() {

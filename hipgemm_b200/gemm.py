@@ -22,9 +22,42 @@ def _ptr(t: torch.Tensor | None) -> int | None:
     return None if t is None else t.data_ptr()
 
 
-def _stream_handle(stream: torch.cuda.Stream | None) -> int | None:
-    s = stream if stream is not None else torch.cuda.current_stream()
-    return s.cuda_stream or None
+def _stream_handle(stream: torch.cuda.Stream | None, device_index: int | None = None) -> int | None:
+    if stream is not None:
+        return stream.cuda_stream or None
+    if device_index is not None and _raw_stream is not None:
+        return _raw_stream(device_index) or None  # no Python Stream object on the hot path
+    return torch.cuda.current_stream().cuda_stream or None
+
+
+# torch's raw current-stream query (a plain int); absent in some builds, then the public API.
+_raw_stream = getattr(torch._C, "_cuda_getCurrentRawStream", None)
+_fns: dict[str, object] = {}
+
+
+def _fn(name: str):
+    """The C function `name`, looked up once."""
+    f = _fns.get(name)
+    if f is None:
+        f = _fns[name] = getattr(lib(), name)
+    return f
+
+
+class _on_device:
+    """Makes `index` the current CUDA device for the call, entering torch's device context
+    only when it is not already current (the common case costs one query)."""
+
+    def __init__(self, index: int):
+        self.ctx = None if torch.cuda.current_device() == index else torch.cuda.device(index)
+
+    def __enter__(self):
+        if self.ctx is not None:
+            self.ctx.__enter__()
+
+    def __exit__(self, *exc):
+        if self.ctx is not None:
+            self.ctx.__exit__(*exc)
+        return False
 
 
 def _check_operand(name: str, t: torch.Tensor) -> None:
@@ -71,10 +104,13 @@ def fp8_gemm_tn(a: torch.Tensor, b: torch.Tensor, scale_a: torch.Tensor | None =
         if not workspace.is_cuda or workspace.device != a.device or not workspace.is_contiguous():
             raise ValueError("workspace must be a contiguous tensor on the operands' device")
         ws_ptr, ws_bytes = workspace.data_ptr(), workspace.numel() * workspace.element_size()
-    with torch.cuda.device(a.device):
-        rc = lib().hgemm_fp8_tn_ex(_ptr(a), _ptr(b), _ptr(out), M, N, K, _ptr(scale_a), _ptr(scale_b),
-                                   _stream_handle(stream), int(config), int(schedule), ws_ptr, ws_bytes)
-    check(rc, "hgemm_fp8_tn")
+    dev = a.device.index
+    with _on_device(dev):
+        rc = _fn("hgemm_fp8_tn_ex")(a.data_ptr(), b.data_ptr(), out.data_ptr(), M, N, K, _ptr(scale_a),
+                                    _ptr(scale_b), _stream_handle(stream, dev), int(config), int(schedule), ws_ptr,
+                                    ws_bytes)
+    if rc:
+        check(rc, "hgemm_fp8_tn")
     return out
 
 
@@ -248,11 +284,13 @@ def fp8_gemm_tn_mx(a: torch.Tensor, b: torch.Tensor, sfa_blocked: torch.Tensor, 
     _check_scale("scale_b", scale_b, a.device)
     if out is None:
         out = torch.empty((M, N), dtype=torch.bfloat16, device=a.device)
-    with torch.cuda.device(a.device):
-        rc = lib().hgemm_fp8_tn_mx_config(a.data_ptr(), b.data_ptr(), out.data_ptr(), M, N, K,
-                                          sfa_blocked.data_ptr(), sfb_blocked.data_ptr(), _ptr(scale_a),
-                                          _ptr(scale_b), config, _stream_handle(stream))
-    check(rc, "hgemm_fp8_tn_mx_config")
+    dev = a.device.index
+    with _on_device(dev):
+        rc = _fn("hgemm_fp8_tn_mx_config")(a.data_ptr(), b.data_ptr(), out.data_ptr(), M, N, K,
+                                           sfa_blocked.data_ptr(), sfb_blocked.data_ptr(), _ptr(scale_a),
+                                           _ptr(scale_b), config, _stream_handle(stream, dev))
+    if rc:
+        check(rc, "hgemm_fp8_tn_mx_config")
     return out
 
 

@@ -136,9 +136,9 @@ def fp8_gemm_tn_rows(a: torch.Tensor, b: torch.Tensor, out: torch.Tensor, row_be
     N = b.shape[0]
     if out.dtype != torch.bfloat16 or tuple(out.shape) != (M, N) or not out.is_contiguous():
         raise ValueError("out must be a contiguous (M, N) bfloat16 tensor")
-    with torch.cuda.device(a.device):
-        rc = lib().hgemm_fp8_tn_rows(_ptr(a), _ptr(b), _ptr(out), M, N, K, int(row_begin), int(row_end),
-                                     _ptr(scale_a), _ptr(scale_b), _stream_handle(stream))
+    with _on_device(a.device.index):
+        rc = _fn("hgemm_fp8_tn_rows")(_ptr(a), _ptr(b), _ptr(out), M, N, K, int(row_begin), int(row_end),
+                                     _ptr(scale_a), _ptr(scale_b), _stream_handle(stream, a.device.index))
     check(rc, "hgemm_fp8_tn_rows")
     return out
 
@@ -190,9 +190,9 @@ def quantize_e4m3(x: torch.Tensor, out: torch.Tensor | None = None, scale: torch
         scale = torch.empty(1, dtype=torch.float32, device=x.device)
     if out.numel() != x.numel() or out.dtype != torch.uint8 or not out.is_contiguous():
         raise ValueError("out must be a contiguous uint8 tensor with x's size")
-    with torch.cuda.device(x.device):
-        rc = lib().hgemm_quantize_e4m3(x.data_ptr(), dt, x.numel(), out.data_ptr(), scale.data_ptr(),
-                                       _stream_handle(stream))
+    with _on_device(x.device.index):
+        rc = _fn("hgemm_quantize_e4m3")(x.data_ptr(), dt, x.numel(), out.data_ptr(), scale.data_ptr(),
+                                       _stream_handle(stream, x.device.index))
     check(rc, "hgemm_quantize_e4m3")
     return out, scale
 
@@ -220,9 +220,9 @@ def quantize_e4m3_delayed(x: torch.Tensor, scale_in: torch.Tensor, out: torch.Te
         amax_out = torch.empty(1, dtype=torch.float32, device=x.device)
     if out.numel() != x.numel() or out.dtype != torch.uint8 or not out.is_contiguous():
         raise ValueError("out must be a contiguous uint8 tensor with x's size")
-    with torch.cuda.device(x.device):
-        rc = lib().hgemm_quantize_e4m3_delayed(x.data_ptr(), dt, x.numel(), out.data_ptr(), scale_in.data_ptr(),
-                                               amax_out.data_ptr(), _stream_handle(stream))
+    with _on_device(x.device.index):
+        rc = _fn("hgemm_quantize_e4m3_delayed")(x.data_ptr(), dt, x.numel(), out.data_ptr(), scale_in.data_ptr(),
+                                               amax_out.data_ptr(), _stream_handle(stream, x.device.index))
     check(rc, "hgemm_quantize_e4m3_delayed")
     return out, amax_out
 
@@ -316,8 +316,8 @@ def quantize_mx_e4m3(x: torch.Tensor, out: torch.Tensor | None = None, sf_out: t
         raise ValueError("out must be a contiguous uint8 tensor with x's size on x's device")
     if sf.numel() < sf_bytes or sf.dtype != torch.uint8 or not sf.is_contiguous() or sf.device != x.device:
         raise ValueError(f"sf_out must be a contiguous uint8 tensor of {sf_bytes} bytes on x's device")
-    with torch.cuda.device(x.device):
-        rc = lib().hgemm_quantize_mx_e4m3(x.data_ptr(), dt, rows, K, q.data_ptr(), sf.data_ptr(),
-                                          _stream_handle(stream))
+    with _on_device(x.device.index):
+        rc = _fn("hgemm_quantize_mx_e4m3")(x.data_ptr(), dt, rows, K, q.data_ptr(), sf.data_ptr(),
+                                          _stream_handle(stream, x.device.index))
     check(rc, "hgemm_quantize_mx_e4m3")
     return q, sf

@@ -58,6 +58,7 @@ _SIGNATURES = {
     "hgemm_fp8_tn_mx": (_i, [_vp, _vp, _vp, _i, _i, _i, _vp, _vp, _vp, _vp, _vp]),
     "hgemm_fp8_tn_mx_config": (_i, [_vp, _vp, _vp, _i, _i, _i, _vp, _vp, _vp, _vp, _i, _vp]),
     "hgemm_mx_num_configs": (_i, []),
+    "hgemm_debug_stalled_gemm": (_i, [_vp, _vp, _vp, _i, _i, _i, _i, _vp]),
     "hgemm_quantize_mx_e4m3": (_i, [_vp, _i, _i, _i, _vp, _vp, _vp]),
     "hgemm_quantize_e4m3_delayed": (_i, [_vp, _i, ctypes.c_size_t, _vp, _vp, _vp, _vp]),
     "hgemm_mx_config_name": (ctypes.c_char_p, [_i]),

@@ -75,6 +75,10 @@ struct GemmParams {
     // atom (row block i, K block j) at offset (i * sf_k_atoms + j) * 512, read through the
     // SfMaps tensor maps.
     int sf_k_atoms;
+    // Test hook (hgemm_debug_stalled_gemm only): the producer registers the first stage's
+    // bytes but issues no copies for it, so that stage never fills and every role's bounded
+    // wait expires; the kernel then records a status, drains and returns.
+    int debug_stall_first_stage;
 };
 
 // MX scale factors as 3-D TMA tensors over the blocked bytes: x = 128 bytes, y = 128-byte
@@ -374,18 +378,22 @@ __global__ void __launch_bounds__(192, 1)
                     const int a_blk = mb * CTAS + static_cast<int>(rank);
                     const int b_blk = nb * S::SFB_ATOMS;
                     const int sf_y = kb * kSfRowsPerAtom;
+                    // (Test hook: the first stage's bytes are expected but never copied.)
+                    const bool stall = p.debug_stall_first_stage && idx == 0 && kb == w.kb_begin;
                     if (leader) {
                         // For a pair: the MMAs that read this stage finished in both CTAs.
                         if (kPair && !first_pass) mbar_arrive_cluster(peer_empty0 + 8 * stage);
                         const uint32_t full = bar_full + 8 * stage;
                         mbar_arrive_expect_tx(full, CTAS * (S::STAGE_BYTES + S::SF_BYTES));
-                        tma_load_2d(a_dst, &tm_a, kb * S::BK, a_row, full);
-                        tma_load_2d(b_dst, &tm_b, kb * S::BK, b_row, full);
-                        if constexpr (MX) {
-                            tma_load_3d(sf_dst, &sfm.a, 0, sf_y, a_blk, full);
-                            tma_load_3d(sf_dst + 512, &sfm.b, 0, sf_y, b_blk, full);
+                        if (!stall) {
+                            tma_load_2d(a_dst, &tm_a, kb * S::BK, a_row, full);
+                            tma_load_2d(b_dst, &tm_b, kb * S::BK, b_row, full);
+                            if constexpr (MX) {
+                                tma_load_3d(sf_dst, &sfm.a, 0, sf_y, a_blk, full);
+                                tma_load_3d(sf_dst + 512, &sfm.b, 0, sf_y, b_blk, full);
+                            }
                         }
-                    } else {
+                    } else if (!stall) {
                         const uint32_t full = full_leader0 + 8 * stage;
                         tma_load_2d_pair(a_dst, &tm_a, kb * S::BK, a_row, full);
                         tma_load_2d_pair(b_dst, &tm_b, kb * S::BK, b_row, full);

@@ -370,7 +370,7 @@ int check_args(const void* A, const void* B, void* C, int M, int N, int K, int c
 // ldc: C's row stride in elements (0: N), so that C can be a block of a wider matrix.
 int run_gemm(const void* A, const void* B, void* C, int M, int N, int K, const float* sa, const float* sb,
              cudaStream_t stream, int config, int schedule, void* workspace, size_t workspace_bytes,
-             void* const* peer_c = nullptr, int n_peer = 0, int ldc = 0) {
+             void* const* peer_c = nullptr, int n_peer = 0, int ldc = 0, int debug_stall = 0) {
     int rc = check_args(A, B, C, M, N, K, config, schedule);
     if (rc != HGEMM_OK || M == 0 || N == 0) return rc;
     if (ldc == 0) ldc = N;
@@ -424,6 +424,7 @@ int run_gemm(const void* A, const void* B, void* C, int M, int N, int K, const f
     p.dp_tiles = sc.dp_tiles;
     p.sk_tiles = sc.sk_tiles;
     p.sk_slots = sc.sk_slots;
+    p.debug_stall_first_stage = debug_stall;
     const SfMaps no_sf{};
     if (sc.sk_tiles == 0) return kc.launch(ta, tb, tc, p, peers, no_sf, sc.grid, stream);
 
@@ -540,6 +541,13 @@ int hgemm_host_mx_sf_to_blocked(const uint8_t* sf, int rows, int K, uint8_t* blo
         }
     }
     return HGEMM_OK;
+}
+
+int hgemm_debug_stalled_gemm(const void* A, const void* B, void* C, int M, int N, int K, int config,
+                             hgemm_stream_t stream) {
+    if (K <= 0) return HGEMM_ERR_INVALID_VALUE;  // the hook needs a first K block to withhold
+    return hg::run_gemm(A, B, C, M, N, K, nullptr, nullptr, reinterpret_cast<cudaStream_t>(stream), config,
+                        HGEMM_SCHEDULE_DATA_PARALLEL, nullptr, 0, nullptr, 0, 0, 1);
 }
 
 int hgemm_fp8_tn(const void* A, const void* B, void* C, int M, int N, int K, const float* d_scale_a,

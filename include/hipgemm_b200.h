@@ -168,6 +168,14 @@ int hgemm_device_status(uint32_t* status_out);
 /* Human-readable text for an HGEMM_* status code (static storage). */
 const char* hgemm_error_string(int code);
 
+/* Test hook for the failure path: runs the GEMM with its first stage's copies withheld (the
+ * stage's barrier expects bytes that never arrive), so every bounded wait in the kernel
+ * expires after its limit (about 2 s).  The kernel records a status (read it, and clear it, with
+ * hgemm_device_status), drains and returns; the context stays usable and C is unspecified.
+ * Not for production use. */
+int hgemm_debug_stalled_gemm(const void* A, const void* B, void* C, int M, int N, int K, int config,
+                             hgemm_stream_t stream);
+
 /* Library version string. */
 const char* hgemm_version(void);
 

@@ -190,3 +190,10 @@ def test_delayed_quantiser_argument_checks():
     assert f(FAKE, 1, 16, FAKE + 8, FAKE, FAKE, None) == hg.HGEMM_ERR_ALIGNMENT
     assert f(FAKE, 0, 16, FAKE, FAKE + 2, FAKE, None) == hg.HGEMM_ERR_ALIGNMENT
     assert f(FAKE, 0, 16, FAKE, FAKE, FAKE + 1, None) == hg.HGEMM_ERR_ALIGNMENT
+
+
+def test_debug_stall_hook_argument_checks():
+    L = hg.lib()
+    assert L.hgemm_debug_stalled_gemm(FAKE, FAKE, FAKE, 8, 8, 0, 0, None) == hg.HGEMM_ERR_INVALID_VALUE  # no K block
+    assert L.hgemm_debug_stalled_gemm(FAKE, FAKE, FAKE, 8, 8, 16, 99, None) == hg.HGEMM_ERR_INVALID_VALUE
+    assert L.hgemm_debug_stalled_gemm(FAKE, FAKE, FAKE, 8, 8, 24, 0, None) == hg.HGEMM_ERR_ALIGNMENT

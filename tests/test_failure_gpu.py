@@ -1,0 +1,45 @@
+"""The failure path on the GPU without a fault.  hgemm_debug_stalled_gemm withholds the copies
+of the first pipeline stage (its barrier expects bytes that never arrive), so every bounded
+wait in the kernel expires after its limit (~2 s).  The kernel must record a role-coded status,
+drain, free tensor memory and return; the host reads the status, and the context stays usable:
+an ordinary GEMM right afterwards is correct and leaves the status clear.  No trap, assert,
+bad address or endless loop is involved."""
+import time
+
+import pytest
+import torch
+
+from tests.gemm_cases import c_bits, check_against_oracle, make_inputs, to_device
+
+pytestmark = pytest.mark.gpu
+
+# role << 8 | site of every bounded wait a stalled first stage can expire first
+# (producer empty, MMA tensor-memory empty, MMA full, epilogue tensor-memory full).
+WAIT_SITES = {0x0101, 0x0201, 0x0202, 0x0301}
+
+
+@pytest.mark.parametrize("config_name", ["bn128_s6", "pair256_s6"])
+def test_bounded_wait_expires_and_context_survives(cuda_device, config_name):
+    import hipgemm_b200 as hg
+    M, N, K = 256, 512, 512
+    A, B, sa, sb = make_inputs(M, N, K)
+    a, b, ta, tb = to_device(A, B, sa, sb)
+    c = torch.empty((M, N), dtype=torch.bfloat16, device="cuda")
+    assert hg.device_status() == 0  # clears any earlier word
+    config = hg.config_names().index(config_name)
+    t0 = time.perf_counter()
+    rc = hg.lib().hgemm_debug_stalled_gemm(a.data_ptr(), b.data_ptr(), c.data_ptr(), M, N, K, config,
+                                           torch.cuda.current_stream().cuda_stream)
+    torch.cuda.synchronize()
+    elapsed = time.perf_counter() - t0
+    assert rc == hg.HGEMM_OK
+    status = hg.device_status()  # read and cleared
+    assert status in WAIT_SITES, hex(status)
+    assert 1.0 < elapsed < 60.0, elapsed  # the waits ran to their ~2 s limit, then returned
+
+    # The context is usable: the same GEMM now runs normally.
+    out = hg.fp8_gemm_tn(a, b, ta, tb, config=config)
+    torch.cuda.synchronize()
+    assert hg.device_status() == 0
+    bad, n, first = check_against_oracle(c_bits(out), A, B, sa, sb)
+    assert bad == 0, f"{bad}/{n} mismatches after the stalled launch (first {first})"

@@ -227,45 +227,54 @@ __device__ __forceinline__ void st_global_v4(float* p, float a, float b, float c
     asm volatile("st.global.v4.f32 [%0], {%1, %2, %3, %4};" ::"l"(p), "f"(a), "f"(b), "f"(c), "f"(d) : "memory");
 }
 
-template <int CTAS, int BN, int STAGES, bool MX = false>
+// KBS: K blocks per stage.  With KBS = 2 every operand arrives in one TMA load per two K
+// blocks (a 3-D box of 128-byte K chunks: two 16-byte-aligned swizzled K-block tiles back to
+// back), and the MX scale factors of both K blocks in one box each: half the TMA instructions
+// per K block, which matters because each costs the TMA unit a fixed time whatever its size.
+template <int CTAS, int BN, int STAGES, bool MX = false, int KBS = 1>
 struct KernelShape {
     static constexpr int BM = 128 * CTAS;   // output tile rows
-    static constexpr int BK = 128;          // bytes of K per stage = one 128-byte swizzle row
+    static constexpr int BK = 128;          // bytes of K per K block = one 128-byte swizzle row
     static constexpr int UMMA_K = 32;
     static constexpr int kNumThreads = 192;  // warp 0 TMA, warp 1 MMA, warps 2-5 epilogue
     static constexpr int B_ROWS = BN / CTAS;  // rows of B this CTA stages per K block
-    static constexpr int A_BYTES = 128 * BK;
-    static constexpr int B_BYTES = B_ROWS * BK;
+    static constexpr int KB_A_BYTES = 128 * BK;  // one K block of this CTA's A rows
+    static constexpr int KB_B_BYTES = B_ROWS * BK;
+    static constexpr int A_BYTES = KBS * KB_A_BYTES;  // per stage
+    static constexpr int B_BYTES = KBS * KB_B_BYTES;
     static constexpr int STAGE_BYTES = A_BYTES + B_BYTES;
     // MX with BN > 128: the scale factors need tensor-memory columns that a second
     // accumulator would take, so there is one accumulator, and the epilogue frees it as soon
     // as the tile sits in registers (bf16), before its stores.
     static constexpr int ACC_BUFS = (MX && BN > 128) ? 1 : 2;
     static constexpr bool EARLY_RELEASE = ACC_BUFS == 1;
+    // MX: per stage, with the operands and on the same barriers (scale factors are
+    // latency-bound: they need the stage ring's full depth), KBS 512-byte atoms for this
+    // CTA's 128 rows of A (one per K block), then KBS per 128 columns of the whole tile (a
+    // pair's CTAs both hold all of B's), column block major: two loads per stage.
+    static constexpr int SFB_ATOMS = (BN + 127) / 128;
+    static constexpr int SF_BYTES = MX ? 512 * (1 + SFB_ATOMS) * KBS : 0;
+    static constexpr int NUM_BARS = 2 * STAGES + 5;  // full, empty, tfull x2, tempty x2, drain
     // bf16 columns per staged epilogue chunk: 64 (128-byte rows, 128-byte swizzle) when
-    // BN allows, else 32 (64-byte rows, 64-byte swizzle; also the one-accumulator MX tile,
-    // to fit four stages).
-    static constexpr int EPI_COLS = (BN % 64 == 0 && !EARLY_RELEASE) ? 64 : 32;
+    // BN allows and the staging fits beside the stage ring, else 32 (64-byte rows, 64-byte
+    // swizzle; also the one-accumulator MX tile, to fit four stages).
+    static constexpr bool EPI64_FITS =
+        STAGES * (STAGE_BYTES + SF_BYTES) + 8 * 32 * 64 * 2 + NUM_BARS * 8 + 16 + 1024 <= 232448;
+    static constexpr int EPI_COLS = (BN % 64 == 0 && !EARLY_RELEASE && EPI64_FITS) ? 64 : 32;
     static constexpr int EPI_BUF_BYTES = 32 * EPI_COLS * 2;  // one warp's 32 rows
     static constexpr int OFF_A = 0;
     static constexpr int OFF_B = OFF_A + STAGES * A_BYTES;
     static constexpr int OFF_EPI = OFF_B + STAGES * B_BYTES;
-    // MX: per stage, with the operands and on the same barriers (scale factors are
-    // latency-bound: they need the stage ring's full depth), one 512-byte atom for this
-    // CTA's 128 rows of A, then one per 128 columns of the whole tile (a pair's CTAs both
-    // hold all of B's): two loads per stage.
-    static constexpr int SFB_ATOMS = (BN + 127) / 128;
-    static constexpr int SF_BYTES = MX ? 512 * (1 + SFB_ATOMS) : 0;
     static constexpr int OFF_SF = OFF_EPI + 4 * 2 * EPI_BUF_BYTES;
     static constexpr int OFF_BAR = OFF_SF + STAGES * SF_BYTES;
-    static constexpr int NUM_BARS = 2 * STAGES + 5;  // full, empty, tfull x2, tempty x2, drain
     static constexpr int OFF_MISC = OFF_BAR + NUM_BARS * 8;
     static constexpr int SMEM_BYTES = OFF_MISC + 16 + 1024;  // + slack to align the base to 1024 B
-    // ACC_BUFS accumulators of BN fp32 columns, plus (MX) per-stage scale-factor columns (4
-    // per 128 rows of A and of B), rounded up to the power of two tcgen05.alloc takes.
+    // ACC_BUFS accumulators of BN fp32 columns, plus (MX) per-K-block scale-factor columns (4
+    // per 128 rows of A and of B) for each K block a stage holds, rounded up to the power of
+    // two tcgen05.alloc takes.
     static constexpr int SF_COLS = MX ? 4 * (1 + SFB_ATOMS) : 0;
     static constexpr int OFF_SF_COL = ACC_BUFS * BN;
-    static constexpr int COLS_USED = ACC_BUFS * BN + STAGES * SF_COLS;
+    static constexpr int COLS_USED = ACC_BUFS * BN + STAGES * KBS * SF_COLS;
     static constexpr uint32_t TMEM_COLS =
         COLS_USED <= 32 ? 32 : (COLS_USED <= 64 ? 64 : (COLS_USED <= 128 ? 128 : (COLS_USED <= 256 ? 256 : 512)));
     static constexpr uint32_t IDESC = idesc_e4m3_f32(BM, BN);
@@ -275,17 +284,20 @@ struct KernelShape {
     static_assert(COLS_USED <= 512, "tensor memory holds 512 columns");
     static_assert(BN % 32 == 0 && BN >= 64 && BN <= 256, "BN must be a multiple of 32 in [64, 256]");
     static_assert(CTAS == 1 || BN % 16 == 0, "M=256 MMAs need N % 16 == 0");
-    static_assert(B_BYTES % 1024 == 0, "B tiles must keep 1024-byte alignment");
+    static_assert(KB_B_BYTES % 1024 == 0, "B tiles must keep 1024-byte alignment");
+    static_assert(KBS == 1 || KBS == 2, "one or two K blocks per stage");
     static_assert((TMEM_COLS & (TMEM_COLS - 1)) == 0, "tensor memory allocations are powers of two");
     static_assert(SMEM_BYTES <= 232448, "exceeds 227 KB of shared memory per CTA");
 };
 
-template <int CTAS, int BN, int STAGES, bool MX = false>
+// KBS = 2 reads A and B through 3-D maps (x = 128 bytes of K, y = row, z = 128-byte K chunk);
+// KBS = 1 through 2-D maps (x = K byte, y = row).
+template <int CTAS, int BN, int STAGES, bool MX = false, int KBS = 1>
 __global__ void __launch_bounds__(192, 1)
     fp8_gemm_tn_sm100(const __grid_constant__ CUtensorMap tm_a, const __grid_constant__ CUtensorMap tm_b,
                       const __grid_constant__ CUtensorMap tm_c, const GemmParams p,
                       const __grid_constant__ PeerOutputs peers, const __grid_constant__ SfMaps sfm) {
-    using S = KernelShape<CTAS, BN, STAGES, MX>;
+    using S = KernelShape<CTAS, BN, STAGES, MX, KBS>;
     extern __shared__ uint8_t smem_raw[];
     // 128-byte swizzle atoms need 1024-byte alignment.
     const uint32_t raw_base = smem_u32(smem_raw);
@@ -365,15 +377,16 @@ __global__ void __launch_bounds__(192, 1)
                 tile_coords(w.tile, p, mb, nb);
                 const int a_row = mb * S::BM + static_cast<int>(rank) * 128;
                 const int b_row = nb * BN + static_cast<int>(rank) * S::B_ROWS;
-                for (int kb = w.kb_begin; kb < w.kb_end; ++kb) {
+                for (int kb = w.kb_begin; kb < w.kb_end; kb += KBS) {
                     if (!mbar_wait<kPair>(bar_empty + 8 * stage, phase ^ 1u, abort_flag, kErrProducerEmpty)) {
                         ok = false;
                         break;
                     }
                     const uint32_t a_dst = base + S::OFF_A + stage * S::A_BYTES;
                     const uint32_t b_dst = base + S::OFF_B + stage * S::B_BYTES;
-                    // MX: this K block's scale factors, A's for this CTA's 128 rows and B's for
-                    // all of the tile's columns (full boxes: rows past M or N read as zeros).
+                    // MX: the stage's scale factors, A's for this CTA's 128 rows and B's for all
+                    // of the tile's columns (full boxes: rows past M or N, or K blocks past K,
+                    // read as zeros; so does the second K block of a stage past K).
                     const uint32_t sf_dst = base + S::OFF_SF + stage * S::SF_BYTES;
                     const int a_blk = mb * CTAS + static_cast<int>(rank);
                     const int b_blk = nb * S::SFB_ATOMS;
@@ -386,20 +399,30 @@ __global__ void __launch_bounds__(192, 1)
                         const uint32_t full = bar_full + 8 * stage;
                         mbar_arrive_expect_tx(full, CTAS * (S::STAGE_BYTES + S::SF_BYTES));
                         if (!stall) {
-                            tma_load_2d(a_dst, &tm_a, kb * S::BK, a_row, full);
-                            tma_load_2d(b_dst, &tm_b, kb * S::BK, b_row, full);
+                            if constexpr (KBS == 1) {
+                                tma_load_2d(a_dst, &tm_a, kb * S::BK, a_row, full);
+                                tma_load_2d(b_dst, &tm_b, kb * S::BK, b_row, full);
+                            } else {
+                                tma_load_3d(a_dst, &tm_a, 0, a_row, kb, full);
+                                tma_load_3d(b_dst, &tm_b, 0, b_row, kb, full);
+                            }
                             if constexpr (MX) {
                                 tma_load_3d(sf_dst, &sfm.a, 0, sf_y, a_blk, full);
-                                tma_load_3d(sf_dst + 512, &sfm.b, 0, sf_y, b_blk, full);
+                                tma_load_3d(sf_dst + 512 * KBS, &sfm.b, 0, sf_y, b_blk, full);
                             }
                         }
                     } else if (!stall) {
                         const uint32_t full = full_leader0 + 8 * stage;
-                        tma_load_2d_pair(a_dst, &tm_a, kb * S::BK, a_row, full);
-                        tma_load_2d_pair(b_dst, &tm_b, kb * S::BK, b_row, full);
+                        if constexpr (KBS == 1) {
+                            tma_load_2d_pair(a_dst, &tm_a, kb * S::BK, a_row, full);
+                            tma_load_2d_pair(b_dst, &tm_b, kb * S::BK, b_row, full);
+                        } else {
+                            tma_load_3d_pair(a_dst, &tm_a, 0, a_row, kb, full);
+                            tma_load_3d_pair(b_dst, &tm_b, 0, b_row, kb, full);
+                        }
                         if constexpr (MX) {
                             tma_load_3d_pair(sf_dst, &sfm.a, 0, sf_y, a_blk, full);
-                            tma_load_3d_pair(sf_dst + 512, &sfm.b, 0, sf_y, b_blk, full);
+                            tma_load_3d_pair(sf_dst + 512 * KBS, &sfm.b, 0, sf_y, b_blk, full);
                         }
                     }
                     if (++stage == STAGES) {
@@ -420,14 +443,16 @@ __global__ void __launch_bounds__(192, 1)
             int acc = 0;
             uint32_t acc_phase = 0;
             bool ok = true;
-            // MX: the scale factors of stage s go to its own tensor-memory columns with
-            // tcgen05.cp, which runs in issue order with the MMAs that read them.
-            auto issue_sf_cp = [&](int s) {
-                const uint32_t tsfa = tmem_base + static_cast<uint32_t>(S::OFF_SF_COL + s * S::SF_COLS);
+            // MX: the scale factors of K block h of stage s go to their own tensor-memory
+            // columns (at tsfa) with tcgen05.cp, which runs in issue order with the MMAs that
+            // read them.  In shared memory A's atom of K block h is at 512 h, B's atom of
+            // column block c at 512 (KBS (1 + c) + h).
+            auto issue_sf_cp = [&](int s, int h, uint32_t tsfa) {
                 const uint32_t sf_src = base + S::OFF_SF + s * S::SF_BYTES;
+                tmem_cp_32x128b_warpx4<CTAS>(tsfa, sf_smem_desc(sf_src + 512 * h));
 #pragma unroll
-                for (int i = 0; i <= S::SFB_ATOMS; ++i) {
-                    tmem_cp_32x128b_warpx4<CTAS>(tsfa + 4 * i, sf_smem_desc(sf_src + 512 * i));
+                for (int c = 0; c < S::SFB_ATOMS; ++c) {
+                    tmem_cp_32x128b_warpx4<CTAS>(tsfa + 4 * (1 + c), sf_smem_desc(sf_src + 512 * (KBS * (1 + c) + h)));
                 }
             };
             Work w;
@@ -438,36 +463,44 @@ __global__ void __launch_bounds__(192, 1)
                 }
                 tc_fence_after();
                 const uint32_t d_tmem = tmem_base + static_cast<uint32_t>(acc * BN);
-                for (int kb = w.kb_begin; kb < w.kb_end; ++kb) {
+                for (int kb = w.kb_begin; kb < w.kb_end; kb += KBS) {
                     if (!mbar_wait<kPair>(bar_full + 8 * stage, phase, abort_flag, kErrMmaFull)) {
                         ok = false;
                         break;
                     }
                     tc_fence_after();
-                    const uint64_t a_desc = sw128_kmajor_desc(base + S::OFF_A + stage * S::A_BYTES);
-                    const uint64_t b_desc = sw128_kmajor_desc(base + S::OFF_B + stage * S::B_BYTES);
-                    if constexpr (MX) {
-                        // Scale factors of this stage: A's at tsfa (4 columns), B's after them.
-                        const uint32_t tsfa = tmem_base + static_cast<uint32_t>(S::OFF_SF_COL + stage * S::SF_COLS);
-                        const uint32_t tsfb = tsfa + 4;
-                        issue_sf_cp(stage);
 #pragma unroll
-                        for (int k = 0; k < S::BK / S::UMMA_K; ++k) {
-                            const uint64_t koff = static_cast<uint64_t>((k * S::UMMA_K) >> 4);
-                            const uint32_t accumulate = (kb > w.kb_begin || k > 0) ? 1u : 0u;
-                            // K slice k uses byte k of each scale-factor column.
-                            const uint32_t sf_id = static_cast<uint32_t>(k);
-                            mma_mxf8f6f4<CTAS>(d_tmem, a_desc + koff, b_desc + koff, idesc_mx_e4m3(S::BM, BN, sf_id),
-                                         tsfa | (sf_id << 30), tsfb | (sf_id << 30), accumulate);
-                        }
-                    } else {
+                    for (int h = 0; h < KBS; ++h) {
+                        if (h > 0 && kb + h >= w.kb_end) break;  // a stage's second K block past the range
+                        const uint64_t a_desc =
+                            sw128_kmajor_desc(base + S::OFF_A + stage * S::A_BYTES + h * S::KB_A_BYTES);
+                        const uint64_t b_desc =
+                            sw128_kmajor_desc(base + S::OFF_B + stage * S::B_BYTES + h * S::KB_B_BYTES);
+                        if constexpr (MX) {
+                            // Scale factors of this K block: A's at tsfa (4 columns), B's after them.
+                            const uint32_t tsfa =
+                                tmem_base + static_cast<uint32_t>(S::OFF_SF_COL + (stage * KBS + h) * S::SF_COLS);
+                            const uint32_t tsfb = tsfa + 4;
+                            issue_sf_cp(stage, h, tsfa);
 #pragma unroll
-                        for (int k = 0; k < S::BK / S::UMMA_K; ++k) {
-                            // Advancing the start address by 32 B walks K inside the swizzle
-                            // atom: the hardware applies the XOR pattern to the final address.
-                            const uint64_t koff = static_cast<uint64_t>((k * S::UMMA_K) >> 4);
-                            const uint32_t accumulate = (kb > w.kb_begin || k > 0) ? 1u : 0u;
-                            mma_f8f6f4<CTAS>(d_tmem, a_desc + koff, b_desc + koff, S::IDESC, accumulate);
+                            for (int k = 0; k < S::BK / S::UMMA_K; ++k) {
+                                const uint64_t koff = static_cast<uint64_t>((k * S::UMMA_K) >> 4);
+                                const uint32_t accumulate = (kb + h > w.kb_begin || k > 0) ? 1u : 0u;
+                                // K slice k uses byte k of each scale-factor column.
+                                const uint32_t sf_id = static_cast<uint32_t>(k);
+                                mma_mxf8f6f4<CTAS>(d_tmem, a_desc + koff, b_desc + koff,
+                                                   idesc_mx_e4m3(S::BM, BN, sf_id), tsfa | (sf_id << 30),
+                                                   tsfb | (sf_id << 30), accumulate);
+                            }
+                        } else {
+#pragma unroll
+                            for (int k = 0; k < S::BK / S::UMMA_K; ++k) {
+                                // Advancing the start address by 32 B walks K inside the swizzle
+                                // atom: the hardware applies the XOR pattern to the final address.
+                                const uint64_t koff = static_cast<uint64_t>((k * S::UMMA_K) >> 4);
+                                const uint32_t accumulate = (kb + h > w.kb_begin || k > 0) ? 1u : 0u;
+                                mma_f8f6f4<CTAS>(d_tmem, a_desc + koff, b_desc + koff, S::IDESC, accumulate);
+                            }
                         }
                     }
                     mma_commit<CTAS>(bar_empty + 8 * stage);  // frees the stage when these MMAs finish

@@ -60,12 +60,13 @@ struct KernelConfig {
     const void* kernel;  // __global__ function pointer
     int (*launch)(const CUtensorMap&, const CUtensorMap&, const CUtensorMap&, const GemmParams&,
                   const PeerOutputs&, const SfMaps&, int grid, cudaStream_t);
+    int kbs;  // K blocks per stage (2: 3-D operand maps, which need K % 128 == 0)
 };
 
-template <int CTAS, int BN, int STAGES, bool MX = false>
+template <int CTAS, int BN, int STAGES, bool MX = false, int KBS = 1>
 int launch_kernel(const CUtensorMap& ta, const CUtensorMap& tb, const CUtensorMap& tc, const GemmParams& p,
                   const PeerOutputs& peers, const SfMaps& sfm, int grid, cudaStream_t stream) {
-    using S = KernelShape<CTAS, BN, STAGES, MX>;
+    using S = KernelShape<CTAS, BN, STAGES, MX, KBS>;
     cudaLaunchConfig_t cfg{};
     cfg.gridDim = dim3(static_cast<unsigned>(grid), 1, 1);
     cfg.blockDim = dim3(S::kNumThreads, 1, 1);
@@ -88,20 +89,21 @@ int launch_kernel(const CUtensorMap& ta, const CUtensorMap& tb, const CUtensorMa
     cfg.attrs = attr;
     cfg.numAttrs = n_attr;
     const cudaError_t e =
-        cudaLaunchKernelEx(&cfg, fp8_gemm_tn_sm100<CTAS, BN, STAGES, MX>, ta, tb, tc, p, peers, sfm);
+        cudaLaunchKernelEx(&cfg, fp8_gemm_tn_sm100<CTAS, BN, STAGES, MX, KBS>, ta, tb, tc, p, peers, sfm);
     return e == cudaSuccess ? HGEMM_OK : HGEMM_ERR_CUDA;
 }
 
-template <int CTAS, int BN, int STAGES, bool MX = false>
+template <int CTAS, int BN, int STAGES, bool MX = false, int KBS = 1>
 KernelConfig make_config(const char* name, double eff) {
-    using S = KernelShape<CTAS, BN, STAGES, MX>;
+    using S = KernelShape<CTAS, BN, STAGES, MX, KBS>;
     return KernelConfig{name,         CTAS,
                         S::BM,        BN,
                         S::B_ROWS,    eff,
                         S::SMEM_BYTES, S::PARTIAL_FLOATS,
                         S::EPI_COLS,
-                        reinterpret_cast<const void*>(&fp8_gemm_tn_sm100<CTAS, BN, STAGES, MX>),
-                        &launch_kernel<CTAS, BN, STAGES, MX>};
+                        reinterpret_cast<const void*>(&fp8_gemm_tn_sm100<CTAS, BN, STAGES, MX, KBS>),
+                        &launch_kernel<CTAS, BN, STAGES, MX, KBS>,
+                        KBS};
 }
 
 const KernelConfig kConfigs[] = {
@@ -117,22 +119,28 @@ constexpr int kNumConfigs = sizeof(kConfigs) / sizeof(kConfigs[0]);
 
 // MX block-scaled kernels (index c + 1 of hgemm_fp8_tn_mx_config; 0 = choose).  256 x 256
 // tiles on CTA pairs and 128 x 256 tiles, both with one accumulator (early release), and
-// 128 x 128 tiles with two for grids too small to fill the GPU with the wide tiles.  eff:
-// measured per-SM throughput at 8192^3 relative to the best config.
+// 128 x 128 tiles with two for grids too small to fill the GPU with the wide tiles.  The
+// "x2" kernels stage two K blocks per TMA load (K % 128 == 0 only): measured at 8192^3 on
+// B200, 620-630 K cycles against 690-705 K for the pair, and +15 % for the 128 x 128 tile;
+// the plain kernel gains nothing from it (515 K cycles either way).  eff: measured per-SM
+// throughput at 8192^3 relative to the best config.
 const KernelConfig kMxConfigs[] = {
-    make_config<1, 256, 4, true>("mx_bn256_s4", 0.95),
-    make_config<1, 128, 5, true>("mx_bn128_s5", 0.52),
-    make_config<2, 256, 6, true>("mx_pair256_s6", 1.0),
+    make_config<1, 256, 4, true>("mx_bn256_s4", 0.85),
+    make_config<1, 128, 5, true>("mx_bn128_s5", 0.51),
+    make_config<2, 256, 6, true>("mx_pair256_s6", 0.90),
+    make_config<2, 256, 3, true, 2>("mx_pair256_s3x2", 1.0),
+    make_config<1, 128, 3, true, 2>("mx_bn128_s3x2", 0.60),
 };
 constexpr int kNumMxConfigs = sizeof(kMxConfigs) / sizeof(kMxConfigs[0]);
 
 // Fewest estimated tile-time units: waves of tiles over the resident slots (CTAs or CTA
 // pairs) times the tile's per-SM MMA work (BM * BN / (128 * 128 * CTAS)) over its efficiency.
-int choose_mx_config(int M, int N, const int* resident_ctas) {
+int choose_mx_config(int M, int N, int K, const int* resident_ctas) {
     int best = 0;
     double best_cost = 0.0;
     for (int c = 0; c < kNumMxConfigs; ++c) {
         const KernelConfig& k = kMxConfigs[c];
+        if (k.kbs > 1 && K % 128 != 0) continue;
         const long long tiles = static_cast<long long>((M + k.bm - 1) / k.bm) * ((N + k.bn - 1) / k.bn);
         const long long slots = resident_ctas[c] / k.ctas;
         if (slots < 1) continue;
@@ -253,13 +261,33 @@ bool encode_2d(CUtensorMap* map, CUtensorMapDataType dtype, size_t elem_bytes, c
                     CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
 }
 
+// An e4m3 operand (rows x K bytes, row-major) for a kernel with `kbs` K blocks per stage.
+// kbs = 1: 2-D, x = K byte, y = row, box 128 x box_rows.  kbs = 2: 3-D, x = byte in a
+// 128-byte K chunk, y = row, z = chunk (stride 128 bytes), box 128 x box_rows x 2, which lands
+// in shared memory as two K-block tiles back to back; needs K % 128 == 0, or the last chunk
+// would read the next row's bytes instead of zeros.
+bool encode_operand(CUtensorMap* map, const void* ptr, int K, int rows, int box_rows, int kbs) {
+    if (kbs == 1) {
+        return encode_2d(map, CU_TENSOR_MAP_DATA_TYPE_UINT8, 1, ptr, static_cast<uint64_t>(K),
+                         static_cast<uint64_t>(rows), 128, static_cast<uint32_t>(box_rows));
+    }
+    const cuuint64_t dims[3] = {128, static_cast<cuuint64_t>(rows), static_cast<cuuint64_t>(K / 128)};
+    const cuuint64_t strides[2] = {static_cast<cuuint64_t>(K), 128};
+    const cuuint32_t box[3] = {128, static_cast<cuuint32_t>(box_rows), static_cast<cuuint32_t>(kbs)};
+    const cuuint32_t estr[3] = {1, 1, 1};
+    return g_encode(map, CU_TENSOR_MAP_DATA_TYPE_UINT8, 3, const_cast<void*>(ptr), dims, strides, box, estr,
+                    CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                    CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
+
 // An MX scale-factor tensor in the blocked layout as a 3-D map: x = 128 bytes, y = k_rows
-// 128-byte rows along K (4 per atom), z = row_blocks 128-row blocks; box 128 x 4 x
-// box_blocks (one K block's atoms).  Out-of-range blocks read as zeros.
-bool encode_sf_3d(CUtensorMap* map, const void* ptr, uint64_t k_rows, uint64_t row_blocks, uint32_t box_blocks) {
+// 128-byte rows along K (4 per atom), z = row_blocks 128-row blocks; box 128 x 4 kbs x
+// box_blocks (the atoms of kbs K blocks).  Out-of-range rows and blocks read as zeros.
+bool encode_sf_3d(CUtensorMap* map, const void* ptr, uint64_t k_rows, uint64_t row_blocks, uint32_t box_blocks,
+                  int kbs) {
     const cuuint64_t dims[3] = {128, k_rows, row_blocks};
     const cuuint64_t strides[2] = {128, k_rows * 128};
-    const cuuint32_t box[3] = {128, static_cast<cuuint32_t>(kSfRowsPerAtom), box_blocks};
+    const cuuint32_t box[3] = {128, static_cast<cuuint32_t>(kSfRowsPerAtom * kbs), box_blocks};
     const cuuint32_t estr[3] = {1, 1, 1};
     return g_encode(map, CU_TENSOR_MAP_DATA_TYPE_UINT8, 3, const_cast<void*>(ptr), dims, strides, box, estr,
                     CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
@@ -335,11 +363,11 @@ Schedule make_schedule(int M, int N, int K, int config, int schedule, const Devi
 // tiles over the resident slots times the per-SM share of one tile ((bm / ctas) x bn per
 // K block), divided by the configuration's measured relative efficiency.
 int choose_config(int M, int N, int K, const DeviceState& dev) {
-    (void)K;
     int best = 1;
     double best_cost = 1e300;
     for (int c = 1; c < kNumConfigs; ++c) {
         const KernelConfig& k = kConfigs[c];
+        if (k.kbs > 1 && K % 128 != 0) continue;
         const Schedule sc = make_schedule(M, N, K, c, HGEMM_SCHEDULE_DATA_PARALLEL, dev);
         const double area = static_cast<double>(k.bm / k.ctas) * k.bn;
         const double work_per_slot = static_cast<double>((sc.tiles + sc.slots - 1) / sc.slots);
@@ -390,14 +418,12 @@ int run_gemm(const void* A, const void* B, void* C, int M, int N, int K, const f
     }
     const int c = config == 0 ? choose_config(M, N, K, *dev) : config;
     const KernelConfig& kc = kConfigs[c];
+    if (kc.kbs > 1 && K % 128 != 0) return HGEMM_ERR_UNSUPPORTED;  // (never chosen automatically then)
     const Schedule sc = make_schedule(M, N, K, c, schedule, *dev);
 
     const CUtensorMapSwizzle c_swizzle = kc.epi_cols == 64 ? CU_TENSOR_MAP_SWIZZLE_128B : CU_TENSOR_MAP_SWIZZLE_64B;
     CUtensorMap ta, tb, tc;
-    if (!encode_2d(&ta, CU_TENSOR_MAP_DATA_TYPE_UINT8, 1, A, static_cast<uint64_t>(K), static_cast<uint64_t>(M), 128,
-                   128) ||
-        !encode_2d(&tb, CU_TENSOR_MAP_DATA_TYPE_UINT8, 1, B, static_cast<uint64_t>(K), static_cast<uint64_t>(N), 128,
-                   static_cast<uint32_t>(kc.b_box_rows)) ||
+    if (!encode_operand(&ta, A, K, M, 128, kc.kbs) || !encode_operand(&tb, B, K, N, kc.b_box_rows, kc.kbs) ||
         !encode_2d(&tc, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, C, static_cast<uint64_t>(N), static_cast<uint64_t>(M),
                    static_cast<uint32_t>(kc.epi_cols), 32, c_swizzle, static_cast<uint64_t>(ldc) * 2)) {
         return HGEMM_ERR_CUDA;
@@ -452,19 +478,18 @@ int run_gemm_mx(const void* A, const void* B, void* C, int M, int N, int K, cons
     if (K % 32 != 0) return HGEMM_ERR_ALIGNMENT;
     if (K > 0 && (!sfa || !sfb)) return HGEMM_ERR_INVALID_VALUE;
     if ((reinterpret_cast<uintptr_t>(sfa) & 15u) || (reinterpret_cast<uintptr_t>(sfb) & 15u)) return HGEMM_ERR_ALIGNMENT;
+    // The two-K-block kernels read A and B as 128-byte K chunks, which needs K % 128 == 0.
+    if (config > 0 && kMxConfigs[config - 1].kbs > 1 && K % 128 != 0) return HGEMM_ERR_UNSUPPORTED;
     const DeviceState* dev = current_device_setup(&rc);
     if (rc != HGEMM_OK) return rc;
     if (K == 0) {
         return cudaMemsetAsync(C, 0, static_cast<size_t>(M) * N * 2, stream) == cudaSuccess ? HGEMM_OK
                                                                                               : HGEMM_ERR_CUDA;
     }
-    const int ci = config > 0 ? config - 1 : choose_mx_config(M, N, dev->mx_resident_ctas);
+    const int ci = config > 0 ? config - 1 : choose_mx_config(M, N, K, dev->mx_resident_ctas);
     const KernelConfig& kc = kMxConfigs[ci];
     CUtensorMap ta, tb, tc;
-    if (!encode_2d(&ta, CU_TENSOR_MAP_DATA_TYPE_UINT8, 1, A, static_cast<uint64_t>(K), static_cast<uint64_t>(M), 128,
-                   128) ||
-        !encode_2d(&tb, CU_TENSOR_MAP_DATA_TYPE_UINT8, 1, B, static_cast<uint64_t>(K), static_cast<uint64_t>(N), 128,
-                   static_cast<uint32_t>(kc.b_box_rows)) ||
+    if (!encode_operand(&ta, A, K, M, 128, kc.kbs) || !encode_operand(&tb, B, K, N, kc.b_box_rows, kc.kbs) ||
         !encode_2d(&tc, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, C, static_cast<uint64_t>(N), static_cast<uint64_t>(M),
                    static_cast<uint32_t>(kc.epi_cols), 32,
                    kc.epi_cols == 64 ? CU_TENSOR_MAP_SWIZZLE_128B : CU_TENSOR_MAP_SWIZZLE_64B)) {
@@ -486,9 +511,9 @@ int run_gemm_mx(const void* A, const void* B, void* C, int M, int N, int K, cons
     // atom along K by 1 (A) or BN / 128 (B) row blocks, no swizzle.
     SfMaps sfm{};
     const uint64_t k_rows = static_cast<uint64_t>(p.sf_k_atoms) * kSfRowsPerAtom;
-    if (!encode_sf_3d(&sfm.a, sfa, k_rows, static_cast<uint64_t>((M + 127) / 128), 1) ||
+    if (!encode_sf_3d(&sfm.a, sfa, k_rows, static_cast<uint64_t>((M + 127) / 128), 1, kc.kbs) ||
         !encode_sf_3d(&sfm.b, sfb, k_rows, static_cast<uint64_t>((N + 127) / 128),
-                      static_cast<uint32_t>(kc.bn / 128))) {
+                      static_cast<uint32_t>(kc.bn / 128), kc.kbs)) {
         return HGEMM_ERR_CUDA;
     }
     const PeerOutputs peers{};

@@ -195,7 +195,9 @@ int hgemm_fp8_tn_mx(const void* A, const void* B, void* C, int M, int N, int K, 
                     const float* d_scale_a, const float* d_scale_b, hgemm_stream_t stream);
 /* hgemm_fp8_tn_mx with its kernel chosen: 0 = by wave count (what hgemm_fp8_tn_mx does),
  * 1 = 128 x 256 tiles, one accumulator; 2 = 128 x 128 tiles; 3 = 256 x 256 tiles on CTA
- * pairs, one accumulator.  Names: hgemm_mx_config_name. */
+ * pairs, one accumulator; 4 and 5 = configs 3 and 2 with two K blocks per TMA load (faster;
+ * K % 128 == 0 only, else HGEMM_ERR_UNSUPPORTED, and config 0 picks them only then).
+ * Names: hgemm_mx_config_name. */
 int hgemm_fp8_tn_mx_config(const void* A, const void* B, void* C, int M, int N, int K, const void* SFA,
                            const void* SFB, const float* d_scale_a, const float* d_scale_b, int config,
                            hgemm_stream_t stream);

@@ -149,12 +149,16 @@ def test_from_host_argument_checks():
 def test_mx_argument_checks():
     L = hg.lib()
     sf = FAKE
-    assert L.hgemm_mx_num_configs() == 4
-    assert [L.hgemm_mx_config_name(c).decode() for c in range(4)] == ["auto", "mx_bn256_s4", "mx_bn128_s5",
-                                                                       "mx_pair256_s6"]
-    assert L.hgemm_mx_config_name(4) is None and L.hgemm_mx_config_name(-1) is None
+    assert L.hgemm_mx_num_configs() == 6
+    assert [L.hgemm_mx_config_name(c).decode() for c in range(6)] == ["auto", "mx_bn256_s4", "mx_bn128_s5",
+                                                                       "mx_pair256_s6", "mx_pair256_s3x2",
+                                                                       "mx_bn128_s3x2"]
+    assert L.hgemm_mx_config_name(6) is None and L.hgemm_mx_config_name(-1) is None
     run = L.hgemm_fp8_tn_mx_config
-    assert run(FAKE, FAKE, FAKE, 8, 8, 64, sf, sf, None, None, 4, None) == hg.HGEMM_ERR_INVALID_VALUE
+    assert run(FAKE, FAKE, FAKE, 8, 8, 64, sf, sf, None, None, 6, None) == hg.HGEMM_ERR_INVALID_VALUE
+    # Two K blocks per load: 128-byte K chunks only.
+    assert run(FAKE, FAKE, FAKE, 8, 8, 160, sf, sf, None, None, 4, None) == hg.HGEMM_ERR_UNSUPPORTED
+    assert run(FAKE, FAKE, FAKE, 8, 8, 96, sf, sf, None, None, 5, None) == hg.HGEMM_ERR_UNSUPPORTED
     assert run(FAKE, FAKE, FAKE, 8, 8, 64, sf, sf, None, None, -1, None) == hg.HGEMM_ERR_INVALID_VALUE
     assert run(FAKE, FAKE, FAKE, 8, 8, 48, sf, sf, None, None, 0, None) == hg.HGEMM_ERR_ALIGNMENT   # K % 32
     assert run(FAKE, FAKE, FAKE, 8, 8, 64, None, sf, None, None, 0, None) == hg.HGEMM_ERR_INVALID_VALUE

@@ -43,11 +43,20 @@ def _mx_operand(rows, K, seed):
     return oracle.quantize_mx(x)
 
 
-@pytest.mark.parametrize("config", [1, 2, 3])
+@pytest.mark.parametrize("config", [1, 2, 3, 4, 5])
 @pytest.mark.parametrize("M,N,K", [(1, 8, 32), (129, 264, 160), (128, 128, 128), (256, 384, 1024), (300, 520, 1056),
-                                   (1000, 1032, 2080), (4096, 4096, 4096)])
+                                   (1000, 1032, 2080), (4096, 4096, 4096), (200, 136, 384), (384, 520, 1152)])
 def test_mx_gemm_matches_oracle(cuda_device, M, N, K, config):
     import hipgemm_b200 as hg
+    if config >= 4 and K % 128 != 0:
+        # Two K blocks per load need whole 128-byte K chunks; the call is refused, nothing runs.
+        with pytest.raises(hg.HgemmError):
+            hg.fp8_gemm_tn_mx(torch.zeros((M, K), dtype=torch.uint8, device="cuda"),
+                              torch.zeros((N, K), dtype=torch.uint8, device="cuda"),
+                              torch.zeros(hg.lib().hgemm_mx_sf_bytes(M, K), dtype=torch.uint8, device="cuda"),
+                              torch.zeros(hg.lib().hgemm_mx_sf_bytes(N, K), dtype=torch.uint8, device="cuda"),
+                              config=config)
+        return
     A, SFA = _mx_operand(M, K, M)
     B, SFB = _mx_operand(N, K, N + 1)
     sfa = hg.mx_sf_to_blocked(torch.from_numpy(SFA), K).cuda()
@@ -82,7 +91,7 @@ def test_mx_unit_scales_equal_plain_gemm(cuda_device):
     plain = hg.fp8_gemm_tn(a, b)
     ref = oracle.gemm(A, B)
     assert oracle.validate(c_bits(plain), ref)[0] == 0
-    for config in (0, 1, 2, 3):
+    for config in (0, 1, 2, 3, 4, 5):
         mx = hg.fp8_gemm_tn_mx(a, b, ones_a, ones_b, config=config)
         assert oracle.validate(c_bits(mx), ref)[0] == 0, config
 
@@ -97,11 +106,16 @@ def test_mx_repeated_calls_identical(cuda_device):
     a, b = torch.from_numpy(A).cuda(), torch.from_numpy(B).cuda()
     sfa = hg.mx_sf_to_blocked(torch.from_numpy(SFA), K).cuda()
     sfb = hg.mx_sf_to_blocked(torch.from_numpy(SFB), K).cuda()
-    for config in (1, 2, 3):
-        first = hg.fp8_gemm_tn_mx(a, b, sfa, sfb, config=config)
+    outs = {}
+    for config in (1, 2, 3, 4, 5):
+        first = outs[config] = hg.fp8_gemm_tn_mx(a, b, sfa, sfb, config=config)
         for _ in range(3):
             assert torch.equal(hg.fp8_gemm_tn_mx(a, b, sfa, sfb, config=config).view(torch.int16),
                                first.view(torch.int16))
+    # Two K blocks per stage issue the same MMAs in the same order as one: same bits.
+    assert torch.equal(outs[4].view(torch.int16), outs[3].view(torch.int16))
+    assert torch.equal(outs[5].view(torch.int16), outs[2].view(torch.int16))
+    first = outs[3]
     rows = sample_rows(M, 24)
     ref = np.concatenate([oracle.gemm_mx(A, B, SFA, SFB, 1.0, 1.0, r, r + 1) for r in rows])
     bad, info = _mismatches(np.ascontiguousarray(c_bits(first)[rows]), ref, _abs_products(A, B, SFA, SFB, rows, 1.0))

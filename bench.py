@@ -62,6 +62,9 @@ def parse_args():
     ap.add_argument("--no-cublas", action="store_true", help="skip the cuBLASLt comparison leg")
     ap.add_argument("--no-cpu", action="store_true", help="skip the CPU baseline leg")
     ap.add_argument("--no-mx", action="store_true", help="skip the MX block-scaled GEMM and quantiser legs")
+    ap.add_argument("--sustained", type=float, default=0.0, metavar="SECONDS",
+                    help="also run our FP8 and MX GEMMs and cuBLASLt's back to back for SECONDS each "
+                         "(timing the second half, SM clock sampled): the power-capped regime (N=1 only)")
     ap.add_argument("--seed", type=int, default=0)
     return ap.parse_args()
 
@@ -294,6 +297,65 @@ def mx_legs(args, hg, m, N, K, std_b, rank, dev, timed, peak, hbm_peak, C, no_cu
     return out
 
 
+def sustained_legs(args, hg, m, N, K, std_b, dev, A, B, SA, SB, C, config) -> dict:
+    """Throughput once the 1 kW power cap binds: each kernel runs back to back for
+    args.sustained seconds on rotating inputs larger than L2; the second half is timed with CUDA
+    events while NVML samples the SM clock.  In this regime energy per GEMM, not cycles, sets
+    the rate, which can order kernels differently from a short loop."""
+    import torch
+
+    nbuf = len(A)
+    MA, MB, FA, FB = [], [], [], []
+    for j in range(4):
+        g = torch.Generator(device=dev)
+        g.manual_seed(args.seed + 7 * j + 101)
+        qa, fa = hg.quantize_mx_e4m3(torch.randn((m, K), generator=g, device=dev, dtype=torch.float32))
+        qb, fb = hg.quantize_mx_e4m3(torch.randn((N, K), generator=g, device=dev, dtype=torch.float32) * std_b)
+        MA.append(qa); MB.append(qb); FA.append(fa); FB.append(fb)
+    e4, e8 = torch.float8_e4m3fn, torch.float8_e8m0fnu
+    kernels = [
+        ("ours_fp8", lambda i: hg.fp8_gemm_tn(A[i % nbuf], B[i % nbuf], SA[i % nbuf], SB[i % nbuf], out=C,
+                                              config=config)),
+        ("cublaslt_fp8", lambda i: torch._scaled_mm(A[i % nbuf].view(e4), B[i % nbuf].view(e4).t(),
+                                                    scale_a=SA[i % nbuf], scale_b=SB[i % nbuf],
+                                                    out_dtype=torch.bfloat16)),
+        ("ours_mx", lambda i: hg.fp8_gemm_tn_mx(MA[i % 4], MB[i % 4], FA[i % 4], FB[i % 4], out=C)),
+        ("cublaslt_mx", lambda i: torch._scaled_mm(MA[i % 4].view(e4), MB[i % 4].view(e4).t(),
+                                                   scale_a=FA[i % 4].view(e8), scale_b=FB[i % 4].view(e8),
+                                                   out_dtype=torch.bfloat16)),
+    ]
+    flops = 2.0 * m * N * K
+    out = {"seconds_each": args.sustained, "what": "back-to-back launches, second half timed, SM clock sampled"}
+    for name, fn in kernels:
+        try:
+            t0 = time.time()
+            n = 0
+            while time.time() - t0 < args.sustained / 2:
+                for j in range(20):
+                    fn(n + j)
+                n += 20
+                torch.cuda.synchronize()
+            sampler = ClockSampler(torch.cuda.current_device(), period_s=0.02)
+            e0 = torch.cuda.Event(enable_timing=True)
+            e1 = torch.cuda.Event(enable_timing=True)
+            sampler.start()
+            e0.record()
+            for j in range(n):
+                fn(j)
+            e1.record()
+            torch.cuda.synchronize()
+            clocks = sampler.stop()
+            ms = e0.elapsed_time(e1) / n
+            out[name] = {"value": flops / (ms * 1e-3) / 1e12, "unit": "TFLOP/s", "launches": n,
+                         "sm_mhz": clocks.get("sm_mhz"), "reasons": clocks.get("reasons")}
+        except Exception as e:  # e.g. a torch build without block-scaled _scaled_mm
+            out[name] = {"unavailable": f"{type(e).__name__}: {str(e).splitlines()[0][:160]}"}
+    if hg.device_status() != 0:
+        raise SystemExit("kernel status word set during the sustained legs: a bounded wait expired")
+    del MA, MB, FA, FB
+    return out
+
+
 def run_ours(args) -> None:
     import torch
     import torch.distributed as dist
@@ -419,6 +481,8 @@ def run_ours(args) -> None:
 
     if not args.no_mx:
         extra.update(mx_legs(args, hg, m, N, K, std_b, rank, dev, timed, peak, hbm_peak, C, no_cublas=args.no_cublas))
+    if args.sustained > 0 and world == 1:
+        extra["sustained"] = sustained_legs(args, hg, m, N, K, std_b, dev, A, B, SA, SB, C, config)
 
     # End to end through the public API: pinned host A/B in, GEMM, C back to pinned host.
     hA = A[0].cpu().pin_memory()

@@ -269,12 +269,15 @@ struct KernelShape {
     static constexpr int OFF_BAR = OFF_SF + STAGES * SF_BYTES;
     static constexpr int OFF_MISC = OFF_BAR + NUM_BARS * 8;
     static constexpr int SMEM_BYTES = OFF_MISC + 16 + 1024;  // + slack to align the base to 1024 B
-    // ACC_BUFS accumulators of BN fp32 columns, plus (MX) per-K-block scale-factor columns (4
-    // per 128 rows of A and of B) for each K block a stage holds, rounded up to the power of
-    // two tcgen05.alloc takes.
+    // ACC_BUFS accumulators of BN fp32 columns, plus (MX) one set of scale-factor columns (4
+    // per 128 rows of A and of B), rounded up to the power of two tcgen05.alloc takes.  Every
+    // K block's copies reuse the same columns: tcgen05.cp and tcgen05.mma execute in issue
+    // order, so a copy lands only after the MMAs issued before it have read the previous
+    // block's factors (measured at 8192^3: 602 K cycles against 627 K with one set per K block
+    // of the ring).
     static constexpr int SF_COLS = MX ? 4 * (1 + SFB_ATOMS) : 0;
     static constexpr int OFF_SF_COL = ACC_BUFS * BN;
-    static constexpr int COLS_USED = ACC_BUFS * BN + STAGES * KBS * SF_COLS;
+    static constexpr int COLS_USED = ACC_BUFS * BN + SF_COLS;
     static constexpr uint32_t TMEM_COLS =
         COLS_USED <= 32 ? 32 : (COLS_USED <= 64 ? 64 : (COLS_USED <= 128 ? 128 : (COLS_USED <= 256 ? 256 : 512)));
     static constexpr uint32_t IDESC = idesc_e4m3_f32(BM, BN);
@@ -443,10 +446,10 @@ __global__ void __launch_bounds__(192, 1)
             int acc = 0;
             uint32_t acc_phase = 0;
             bool ok = true;
-            // MX: the scale factors of K block h of stage s go to their own tensor-memory
-            // columns (at tsfa) with tcgen05.cp, which runs in issue order with the MMAs that
-            // read them.  In shared memory A's atom of K block h is at 512 h, B's atom of
-            // column block c at 512 (KBS (1 + c) + h).
+            // MX: the scale factors of K block h of stage s go to the scale-factor columns (at
+            // tsfa) with tcgen05.cp, which runs in issue order with the MMAs that read them.  In
+            // shared memory A's atom of K block h is at 512 h, B's atom of column block c at
+            // 512 (KBS (1 + c) + h).
             auto issue_sf_cp = [&](int s, int h, uint32_t tsfa) {
                 const uint32_t sf_src = base + S::OFF_SF + s * S::SF_BYTES;
                 tmem_cp_32x128b_warpx4<CTAS>(tsfa, sf_smem_desc(sf_src + 512 * h));
@@ -478,8 +481,7 @@ __global__ void __launch_bounds__(192, 1)
                             sw128_kmajor_desc(base + S::OFF_B + stage * S::B_BYTES + h * S::KB_B_BYTES);
                         if constexpr (MX) {
                             // Scale factors of this K block: A's at tsfa (4 columns), B's after them.
-                            const uint32_t tsfa =
-                                tmem_base + static_cast<uint32_t>(S::OFF_SF_COL + (stage * KBS + h) * S::SF_COLS);
+                            const uint32_t tsfa = tmem_base + static_cast<uint32_t>(S::OFF_SF_COL);
                             const uint32_t tsfb = tsfa + 4;
                             issue_sf_cp(stage, h, tsfa);
 #pragma unroll

@@ -75,6 +75,10 @@ struct GemmParams {
     // atom (row block i, K block j) at offset (i * sf_k_atoms + j) * 512, read through the
     // SfMaps tensor maps.
     int sf_k_atoms;
+    // Split-K clusters (the SPLIT > 1 kernels only; 1 otherwise): CTA r of each cluster of
+    // split_k CTAs computes K blocks [r KB / split_k, (r + 1) KB / split_k) of tile
+    // blockIdx.x / split_k, and the cluster sums the partials through distributed shared memory.
+    int split_k;
     // Test hook (hgemm_debug_stalled_gemm only): the producer registers the first stage's
     // bytes but issues no copies for it, so that stage never fills and every role's bounded
     // wait expires; the kernel then records a status, drains and returns.
@@ -107,6 +111,8 @@ enum : uint32_t {
     kErrMmaFull = 0x0202,
     kErrMmaDrain = 0x0203,
     kErrEpiTmemFull = 0x0301,
+    kErrSplitFree = 0x0302,  // split-K: a peer's receive buffer never became free
+    kErrSplitFull = 0x0303,  // split-K: the peers' partial rows never all arrived
 };
 
 // Output tile -> (m block, n block) with GROUP_M tile rows per raster group: inside a
@@ -140,8 +146,18 @@ __host__ __device__ __forceinline__ long long sk_begin(const GemmParams& p, int 
 //      shared tiles run while the MMAs continue with whole tiles;
 //   2. whole tiles of its stream-K range;
 //   3. its data-parallel tiles slot, slot + nslots, ...
+// Split-K clusters (p.split_k > 1) instead: one item per CTA, its K part of one tile (piece 2).
 __host__ __device__ __forceinline__ bool get_work(const GemmParams& p, int slot, int nslots, int idx, Work& w) {
     const int KB = p.num_k_blocks;
+    if (p.split_k > 1) {
+        if (idx > 0) return false;
+        const int part = slot % p.split_k;
+        w.tile = slot / p.split_k;
+        w.kb_begin = static_cast<int>(static_cast<long long>(part) * KB / p.split_k);
+        w.kb_end = static_cast<int>(static_cast<long long>(part + 1) * KB / p.split_k);
+        w.piece = 2;
+        return w.tile < p.dp_tiles;
+    }
     int n_part = 0, n_full = 0, t_first = 0, t_last = -1;
     long long u0 = 0, u1 = 0;
     bool first_partial = false, last_partial = false;
@@ -231,7 +247,8 @@ __device__ __forceinline__ void st_global_v4(float* p, float a, float b, float c
 // blocks (a 3-D box of 128-byte K chunks: two 16-byte-aligned swizzled K-block tiles back to
 // back), and the MX scale factors of both K blocks in one box each: half the TMA instructions
 // per K block, which matters because each costs the TMA unit a fixed time whatever its size.
-template <int CTAS, int BN, int STAGES, bool MX = false, int KBS = 1>
+// SPLIT > 1: split-K over a cluster of SPLIT single CTAs (see the epilogue).
+template <int CTAS, int BN, int STAGES, bool MX = false, int KBS = 1, int SPLIT = 1>
 struct KernelShape {
     static constexpr int BM = 128 * CTAS;   // output tile rows
     static constexpr int BK = 128;          // bytes of K per K block = one 128-byte swizzle row
@@ -254,13 +271,14 @@ struct KernelShape {
     // pair's CTAs both hold all of B's), column block major: two loads per stage.
     static constexpr int SFB_ATOMS = (BN + 127) / 128;
     static constexpr int SF_BYTES = MX ? 512 * (1 + SFB_ATOMS) * KBS : 0;
-    static constexpr int NUM_BARS = 2 * STAGES + 5;  // full, empty, tfull x2, tempty x2, drain
+    // full, empty, tfull x2, tempty x2, drain (+ split-K: receive buffer free, partials in)
+    static constexpr int NUM_BARS = 2 * STAGES + 5 + (SPLIT > 1 ? 2 : 0);
     // bf16 columns per staged epilogue chunk: 64 (128-byte rows, 128-byte swizzle) when
     // BN allows and the staging fits beside the stage ring, else 32 (64-byte rows, 64-byte
     // swizzle; also the one-accumulator MX tile, to fit four stages).
     static constexpr bool EPI64_FITS =
         STAGES * (STAGE_BYTES + SF_BYTES) + 8 * 32 * 64 * 2 + NUM_BARS * 8 + 16 + 1024 <= 232448;
-    static constexpr int EPI_COLS = (BN % 64 == 0 && !EARLY_RELEASE && EPI64_FITS) ? 64 : 32;
+    static constexpr int EPI_COLS = (BN % 64 == 0 && !EARLY_RELEASE && EPI64_FITS && SPLIT == 1) ? 64 : 32;
     static constexpr int EPI_BUF_BYTES = 32 * EPI_COLS * 2;  // one warp's 32 rows
     static constexpr int OFF_A = 0;
     static constexpr int OFF_B = OFF_A + STAGES * A_BYTES;
@@ -289,18 +307,37 @@ struct KernelShape {
     static_assert(CTAS == 1 || BN % 16 == 0, "M=256 MMAs need N % 16 == 0");
     static_assert(KB_B_BYTES % 1024 == 0, "B tiles must keep 1024-byte alignment");
     static_assert(KBS == 1 || KBS == 2, "one or two K blocks per stage");
+    // Split-K: each CTA of the cluster finishes SPLIT_ROWS rows of the tile (SPLIT_QUADS
+    // epilogue warps' worth).  Its stage ring, idle once its MMAs are done, holds
+    //   [0, RECV_BYTES): the peers' fp32 partials of those rows, one 32-row block
+    //       (WARP_BLOCK_BYTES) per (peer, row group), peers in rank order without itself;
+    //   [RECV_BYTES, + RECV_BYTES): its own partial rows for the other ranks, staged by the
+    //       warps that hold them and sent with one bulk copy per warp.
+    // A block is column-chunk major (chunk c of 32 columns at 4096 c, 128 bytes per row); inside
+    // a chunk, row r's 16-byte unit u sits at unit u ^ (r & 7): eight lanes (rows) touching the
+    // same unit hit eight different bank groups.
+    static constexpr int SPLIT_ROWS = 128 / SPLIT;
+    static constexpr int SPLIT_QUADS = SPLIT_ROWS / 32;
+    static constexpr int WARP_BLOCK_BYTES = 32 * BN * 4;
+    static constexpr int RECV_BYTES = SPLIT > 1 ? (SPLIT - 1) * SPLIT_QUADS * WARP_BLOCK_BYTES : 0;
+    static constexpr uint32_t SPLIT_TX_BYTES = static_cast<uint32_t>(RECV_BYTES);
+    static_assert(SPLIT == 1 || SPLIT == 2 || SPLIT == 4, "split-K clusters of 2 or 4");
+    static_assert(SPLIT == 1 || (CTAS == 1 && !MX && KBS == 1), "split-K: single-CTA plain tiles");
+    static_assert(2 * RECV_BYTES <= STAGES * STAGE_BYTES, "receive and send blocks live in the stage ring");
+    static_assert(BN % 32 == 0 || SPLIT == 1, "split-K rows travel in 32-column chunks");
+    static_assert(SPLIT == 1 || (BN / 32 <= 8 && EPI_BUF_BYTES == 32 * 32 * 2), "split-K stores 32 x 32 chunks");
     static_assert((TMEM_COLS & (TMEM_COLS - 1)) == 0, "tensor memory allocations are powers of two");
     static_assert(SMEM_BYTES <= 232448, "exceeds 227 KB of shared memory per CTA");
 };
 
 // KBS = 2 reads A and B through 3-D maps (x = 128 bytes of K, y = row, z = 128-byte K chunk);
 // KBS = 1 through 2-D maps (x = K byte, y = row).
-template <int CTAS, int BN, int STAGES, bool MX = false, int KBS = 1>
+template <int CTAS, int BN, int STAGES, bool MX = false, int KBS = 1, int SPLIT = 1>
 __global__ void __launch_bounds__(192, 1)
     fp8_gemm_tn_sm100(const __grid_constant__ CUtensorMap tm_a, const __grid_constant__ CUtensorMap tm_b,
                       const __grid_constant__ CUtensorMap tm_c, const GemmParams p,
                       const __grid_constant__ PeerOutputs peers, const __grid_constant__ SfMaps sfm) {
-    using S = KernelShape<CTAS, BN, STAGES, MX, KBS>;
+    using S = KernelShape<CTAS, BN, STAGES, MX, KBS, SPLIT>;
     extern __shared__ uint8_t smem_raw[];
     // 128-byte swizzle atoms need 1024-byte alignment.
     const uint32_t raw_base = smem_u32(smem_raw);
@@ -319,6 +356,8 @@ __global__ void __launch_bounds__(192, 1)
     const uint32_t bar_tfull = bar_empty + STAGES * 8;
     const uint32_t bar_tempty = bar_tfull + 2 * 8;
     const uint32_t bar_drain = bar_tempty + 2 * 8;
+    const uint32_t bar_skfree = bar_drain + 8;   // split-K: peers' receive buffers free (SPLIT - 1 arrivals)
+    const uint32_t bar_skfull = bar_skfree + 8;  // split-K: this CTA's rows in from every peer (tx bytes)
     const uint32_t tmem_slot = base + S::OFF_MISC;
     volatile uint32_t* const tmem_slot_ptr = reinterpret_cast<volatile uint32_t*>(smem_gen + S::OFF_MISC);
     volatile uint32_t* const abort_flag = reinterpret_cast<volatile uint32_t*>(smem_gen + S::OFF_MISC + 4);
@@ -334,6 +373,10 @@ __global__ void __launch_bounds__(192, 1)
             mbar_init(bar_tempty + 8 * a, kPair ? 8 : 4);  // one arrive per epilogue warp
         }
         mbar_init(bar_drain, 1);
+        if constexpr (SPLIT > 1) {
+            mbar_init(bar_skfree, SPLIT - 1);
+            mbar_init(bar_skfull, 1);
+        }
         *abort_flag = 0u;
         fence_mbarrier_init();
         fence_proxy_async_smem();
@@ -350,8 +393,8 @@ __global__ void __launch_bounds__(192, 1)
         tmem_relinquish<CTAS>();
     }
     tc_fence_before();
-    if constexpr (kPair) {
-        cluster_sync();  // both CTAs' barriers initialised, tensor memory allocated
+    if constexpr (kPair || SPLIT > 1) {
+        cluster_sync();  // every CTA's barriers initialised (peers signal them), tensor memory allocated
     } else {
         __syncthreads();
     }
@@ -616,6 +659,167 @@ __global__ void __launch_bounds__(192, 1)
             const int row0 = mb * S::BM + static_cast<int>(rank) * 128 + static_cast<int>(quad) * 32;
             const uint32_t tmem_row = tmem_base + ((quad * 32u) << 16) + static_cast<uint32_t>(acc * BN);
 
+            if constexpr (SPLIT > 1) {
+                // ---- split-K: this CTA holds K part `krank` of the whole 128 x BN tile ----
+                // 1. Its stage ring is idle (its MMAs are done): expect the peers' partials of the
+                //    rows it finishes, then tell every peer it may send them.
+                // 2. Once every peer's ring is idle, each warp whose rows another rank finishes
+                //    stages them (swizzled) and sends them with one bulk copy.
+                // 3. Once every peer's rows are in, all four warps fold the peers' partials into
+                //    one (rank order); the warps holding this rank's rows add their own partial
+                //    from tensor memory, scale, round and store.  The order is fixed, so the
+                //    result is the same on every call.
+                const uint32_t krank = cluster_ctarank();
+                if (epi_tid == 0) {
+                    // Expect the peers' bytes before any peer can learn that it may send them.
+                    mbar_arrive_expect_tx(bar_skfull, S::SPLIT_TX_BYTES);
+#pragma unroll
+                    for (uint32_t o = 0; o < static_cast<uint32_t>(SPLIT); ++o) {
+                        if (o != krank) mbar_arrive_cluster_release(mapa_shared(bar_skfree, o));
+                    }
+                }
+                bool ok = mbar_wait<true>(bar_skfree, 0, abort_flag, kErrSplitFree);
+                ok = named_bar_all(1, 128, __all_sync(0xffffffffu, ok));
+                if (!ok) break;
+                const uint32_t owner = quad / static_cast<uint32_t>(S::SPLIT_QUADS);
+                const bool empty_part = w.kb_begin >= w.kb_end;  // fewer K blocks than ranks: zeros
+                constexpr int NC = BN / 32;
+                // Byte offset of row `lane`'s 16-byte unit u of chunk c inside a block.
+                auto swz = [&](int c, uint32_t u) {
+                    return static_cast<uint32_t>(c * 4096) + lane * 128u + (((u ^ lane) & 7u) << 4);
+                };
+                if (owner != krank) {
+                    // Stage chunk c while chunk c + 1 loads from tensor memory, then send it.
+                    const uint32_t first_own_quad = krank * S::SPLIT_QUADS;
+                    const uint32_t send_idx = quad < first_own_quad ? quad : quad - S::SPLIT_QUADS;
+                    const uint32_t stage_blk = base + S::OFF_A + S::RECV_BYTES + send_idx * S::WARP_BLOCK_BYTES;
+                    // This rank's slot among the owner's peers, and the warp's row group there.
+                    const uint32_t slot = krank < owner ? krank : krank - 1u;
+                    const uint32_t group = quad - owner * S::SPLIT_QUADS;
+                    const uint32_t dst_blk = mapa_shared(
+                        base + S::OFF_A + (slot * S::SPLIT_QUADS + group) * S::WARP_BLOCK_BYTES, owner);
+                    const uint32_t dst_bar = mapa_shared(bar_skfull, owner);
+                    uint32_t ra[32], rb[32];
+                    tmem_ld_32x32b_x32(tmem_row, ra);
+#pragma unroll
+                    for (int c = 0; c < NC; ++c) {
+                        uint32_t(&cur)[32] = (c & 1) ? rb : ra;
+                        uint32_t(&nxt)[32] = (c & 1) ? ra : rb;
+                        tmem_ld_wait(cur);
+                        if (c + 1 < NC) tmem_ld_32x32b_x32(tmem_row + (c + 1) * 32, nxt);
+#pragma unroll
+                        for (int j = 0; j < 8; ++j) {
+                            const uint32_t a = stage_blk + swz(c, static_cast<uint32_t>(j));
+                            if (empty_part) {
+                                st_shared_v4(a, 0u, 0u, 0u, 0u);
+                            } else {
+                                st_shared_v4(a, cur[4 * j], cur[4 * j + 1], cur[4 * j + 2], cur[4 * j + 3]);
+                            }
+                        }
+                    }
+                    fence_proxy_async_smem();  // the staged rows are visible to the bulk copy
+                    __syncwarp();
+                    if (lane == 0) bulk_copy_to_peer(dst_blk, stage_blk, S::WARP_BLOCK_BYTES, dst_bar);
+                }
+                ok = mbar_wait<true>(bar_skfull, 0, abort_flag, kErrSplitFull);
+                ok = named_bar_all(1, 128, __all_sync(0xffffffffu, ok));
+                if (!ok) break;
+                const uint32_t recv0 = base + S::OFF_A;
+                if constexpr (SPLIT > 2) {
+                    // All four warps fold the peers' partials (slots in rank order) into slot 0.
+#pragma unroll 1
+                    for (int item = static_cast<int>(epi_idx); item < S::SPLIT_QUADS * NC; item += 4) {
+                        const uint32_t g = static_cast<uint32_t>(item / NC);
+                        const int c = item % NC;
+                        float a[SPLIT - 1][32];
+#pragma unroll
+                        for (int s = 0; s < SPLIT - 1; ++s) {
+#pragma unroll
+                            for (int j = 0; j < 8; ++j) {
+                                ld_shared_v4f(recv0 + (s * S::SPLIT_QUADS + g) * S::WARP_BLOCK_BYTES +
+                                                  swz(c, static_cast<uint32_t>(j)),
+                                              a[s][4 * j], a[s][4 * j + 1], a[s][4 * j + 2], a[s][4 * j + 3]);
+                            }
+                        }
+#pragma unroll
+                        for (int s = 1; s < SPLIT - 1; ++s) {
+#pragma unroll
+                            for (int j = 0; j < 32; ++j) a[0][j] += a[s][j];
+                        }
+#pragma unroll
+                        for (int j = 0; j < 8; ++j) {
+                            st_shared_v4(recv0 + g * S::WARP_BLOCK_BYTES + swz(c, static_cast<uint32_t>(j)),
+                                         __float_as_uint(a[0][4 * j]), __float_as_uint(a[0][4 * j + 1]),
+                                         __float_as_uint(a[0][4 * j + 2]), __float_as_uint(a[0][4 * j + 3]));
+                        }
+                    }
+                    named_bar_sync(1, 128);
+                }
+                if (owner == krank) {
+                    // Peers' sum, then this rank's own partial from tensor memory: a fixed order.
+                    // The warps storing here share the eight epilogue staging buffers (no other
+                    // warp stores), so a chunk's store waits only for one NB chunks back.
+                    const uint32_t group = quad - owner * S::SPLIT_QUADS;
+                    const uint32_t sum_blk = recv0 + group * S::WARP_BLOCK_BYTES;
+                    const int out_row0 = mb * S::BM + static_cast<int>(quad) * 32;
+                    constexpr int NB = 8 / S::SPLIT_QUADS;
+                    const uint32_t buf0 = base + S::OFF_EPI + group * NB * S::EPI_BUF_BYTES;
+                    uint32_t ra[32], rb[32];
+                    tmem_ld_32x32b_x32(tmem_row, ra);
+#pragma unroll
+                    for (int c = 0; c < NC; ++c) {
+                        uint32_t(&cur)[32] = (c & 1) ? rb : ra;
+                        uint32_t(&nxt)[32] = (c & 1) ? ra : rb;
+                        tmem_ld_wait(cur);
+                        if (c + 1 < NC) tmem_ld_32x32b_x32(tmem_row + (c + 1) * 32, nxt);
+                        float v[32];
+#pragma unroll
+                        for (int j = 0; j < 8; ++j) {
+                            ld_shared_v4f(sum_blk + swz(c, static_cast<uint32_t>(j)), v[4 * j], v[4 * j + 1],
+                                          v[4 * j + 2], v[4 * j + 3]);
+                        }
+                        if (!empty_part) {
+#pragma unroll
+                            for (int j = 0; j < 32; ++j) v[j] += __uint_as_float(cur[j]);
+                        }
+                        // Scale, round and stage (64-byte swizzle: 16-byte group q of row `lane` at
+                        // q ^ ((lane / 2) % 4)); every NB chunks (or at the end) one fence, then
+                        // their TMA stores.
+                        const uint32_t buf = buf0 + static_cast<uint32_t>((c % NB) * S::EPI_BUF_BYTES);
+                        if (c >= NB && c % NB == 0) {
+                            if (lane == 0) bulk_wait_group_read<0>();  // the previous round's stores read
+                            __syncwarp();
+                        }
+#pragma unroll
+                        for (int q = 0; q < 4; ++q) {
+                            const uint32_t slot16 = static_cast<uint32_t>(q) ^ ((lane >> 1) & 3u);
+                            st_shared_v4(buf + lane * 64u + slot16 * 16u,
+                                         pack_bf16x2_rn(__fmul_rn(v[8 * q], s), __fmul_rn(v[8 * q + 1], s)),
+                                         pack_bf16x2_rn(__fmul_rn(v[8 * q + 2], s), __fmul_rn(v[8 * q + 3], s)),
+                                         pack_bf16x2_rn(__fmul_rn(v[8 * q + 4], s), __fmul_rn(v[8 * q + 5], s)),
+                                         pack_bf16x2_rn(__fmul_rn(v[8 * q + 6], s), __fmul_rn(v[8 * q + 7], s)));
+                        }
+                        if (c % NB == NB - 1 || c == NC - 1) {
+                            fence_proxy_async_smem();
+                            __syncwarp();
+                            if (lane == 0) {
+                                for (int cc = c - c % NB; cc <= c; ++cc) {
+                                    const int col0 = nb * BN + cc * 32;
+                                    const uint32_t src = buf0 + static_cast<uint32_t>((cc % NB) * S::EPI_BUF_BYTES);
+                                    if (out_row0 < p.M && col0 < p.N) {
+                                        tma_store_2d(&tm_c, col0, out_row0, src);
+                                        for (int i = 0; i < peers.count; ++i) {
+                                            tma_store_2d(&peers.maps[i], col0, out_row0, src);
+                                        }
+                                    }
+                                }
+                                bulk_commit_group();
+                            }
+                        }
+                    }
+                }
+                continue;
+            }
             if constexpr (S::EARLY_RELEASE) {
                 // Drain the row as bf16, then free the accumulator for the next tile's MMAs
                 // while this one is stored (data-parallel tiles only).  The first two chunks
@@ -747,8 +951,8 @@ __global__ void __launch_bounds__(192, 1)
     }
 
     tc_fence_before();
-    if constexpr (kPair) {
-        cluster_sync();  // no CTA leaves while its peer may still signal its barriers
+    if constexpr (kPair || SPLIT > 1) {
+        cluster_sync();  // no CTA leaves while a peer may still signal its barriers or write its memory
     } else {
         __syncthreads();
     }

@@ -60,13 +60,14 @@ struct KernelConfig {
     const void* kernel;  // __global__ function pointer
     int (*launch)(const CUtensorMap&, const CUtensorMap&, const CUtensorMap&, const GemmParams&,
                   const PeerOutputs&, const SfMaps&, int grid, cudaStream_t);
-    int kbs;  // K blocks per stage (2: 3-D operand maps, which need K % 128 == 0)
+    int kbs;    // K blocks per stage (2: 3-D operand maps, which need K % 128 == 0)
+    int split;  // > 1: split-K over clusters of `split` CTAs, one tile per cluster
 };
 
-template <int CTAS, int BN, int STAGES, bool MX = false, int KBS = 1>
+template <int CTAS, int BN, int STAGES, bool MX = false, int KBS = 1, int SPLIT = 1>
 int launch_kernel(const CUtensorMap& ta, const CUtensorMap& tb, const CUtensorMap& tc, const GemmParams& p,
                   const PeerOutputs& peers, const SfMaps& sfm, int grid, cudaStream_t stream) {
-    using S = KernelShape<CTAS, BN, STAGES, MX, KBS>;
+    using S = KernelShape<CTAS, BN, STAGES, MX, KBS, SPLIT>;
     cudaLaunchConfig_t cfg{};
     cfg.gridDim = dim3(static_cast<unsigned>(grid), 1, 1);
     cfg.blockDim = dim3(S::kNumThreads, 1, 1);
@@ -74,9 +75,9 @@ int launch_kernel(const CUtensorMap& ta, const CUtensorMap& tb, const CUtensorMa
     cfg.stream = stream;
     cudaLaunchAttribute attr[2];
     unsigned n_attr = 0;
-    if (CTAS == 2) {
+    if (CTAS * SPLIT > 1) {
         attr[n_attr].id = cudaLaunchAttributeClusterDimension;
-        attr[n_attr].val.clusterDim.x = CTAS;
+        attr[n_attr].val.clusterDim.x = CTAS * SPLIT;
         attr[n_attr].val.clusterDim.y = 1;
         attr[n_attr].val.clusterDim.z = 1;
         ++n_attr;
@@ -89,21 +90,21 @@ int launch_kernel(const CUtensorMap& ta, const CUtensorMap& tb, const CUtensorMa
     cfg.attrs = attr;
     cfg.numAttrs = n_attr;
     const cudaError_t e =
-        cudaLaunchKernelEx(&cfg, fp8_gemm_tn_sm100<CTAS, BN, STAGES, MX, KBS>, ta, tb, tc, p, peers, sfm);
+        cudaLaunchKernelEx(&cfg, fp8_gemm_tn_sm100<CTAS, BN, STAGES, MX, KBS, SPLIT>, ta, tb, tc, p, peers, sfm);
     return e == cudaSuccess ? HGEMM_OK : HGEMM_ERR_CUDA;
 }
 
-template <int CTAS, int BN, int STAGES, bool MX = false, int KBS = 1>
+template <int CTAS, int BN, int STAGES, bool MX = false, int KBS = 1, int SPLIT = 1>
 KernelConfig make_config(const char* name, double eff) {
-    using S = KernelShape<CTAS, BN, STAGES, MX, KBS>;
+    using S = KernelShape<CTAS, BN, STAGES, MX, KBS, SPLIT>;
     return KernelConfig{name,         CTAS,
                         S::BM,        BN,
                         S::B_ROWS,    eff,
                         S::SMEM_BYTES, S::PARTIAL_FLOATS,
                         S::EPI_COLS,
-                        reinterpret_cast<const void*>(&fp8_gemm_tn_sm100<CTAS, BN, STAGES, MX, KBS>),
-                        &launch_kernel<CTAS, BN, STAGES, MX, KBS>,
-                        KBS};
+                        reinterpret_cast<const void*>(&fp8_gemm_tn_sm100<CTAS, BN, STAGES, MX, KBS, SPLIT>),
+                        &launch_kernel<CTAS, BN, STAGES, MX, KBS, SPLIT>,
+                        KBS,          SPLIT};
 }
 
 const KernelConfig kConfigs[] = {
@@ -114,6 +115,8 @@ const KernelConfig kConfigs[] = {
     make_config<2, 256, 6>("pair256_s6", 1.0),
     make_config<2, 128, 8>("pair128_s8", 0.62),
     make_config<2, 224, 6>("pair224_s6", 0.90),
+    make_config<1, 128, 6, false, 1, 2>("bn128_s6_k2", 0.85),
+    make_config<1, 128, 6, false, 1, 4>("bn128_s6_k4", 0.70),
 };
 constexpr int kNumConfigs = sizeof(kConfigs) / sizeof(kConfigs[0]);
 
@@ -187,14 +190,15 @@ int device_setup(int dev) {
                 cudaSuccess) {
                 return 0;
             }
-            if (k.ctas == 1) return prop.multiProcessorCount;
+            const int csize = k.ctas * k.split;  // CTAs per cluster
+            if (csize == 1) return prop.multiProcessorCount;
             cudaLaunchConfig_t cfg{};
             cudaLaunchAttribute attr[1];
             attr[0].id = cudaLaunchAttributeClusterDimension;
-            attr[0].val.clusterDim.x = k.ctas;
+            attr[0].val.clusterDim.x = csize;
             attr[0].val.clusterDim.y = 1;
             attr[0].val.clusterDim.z = 1;
-            cfg.gridDim = dim3(static_cast<unsigned>(k.ctas * (prop.multiProcessorCount / k.ctas)), 1, 1);
+            cfg.gridDim = dim3(static_cast<unsigned>(csize * (prop.multiProcessorCount / csize)), 1, 1);
             cfg.blockDim = dim3(192, 1, 1);
             cfg.dynamicSmemBytes = static_cast<size_t>(k.smem_bytes);
             cfg.attrs = attr;
@@ -204,7 +208,7 @@ int device_setup(int dev) {
                 cudaGetLastError();
                 return 0;
             }
-            return clusters * k.ctas;
+            return clusters * csize;
         };
         for (int c = 1; c < kNumConfigs; ++c) {
             st.resident_ctas[c] = resident(kConfigs[c]);
@@ -348,6 +352,14 @@ Schedule make_schedule(int M, int N, int K, int config, int schedule, const Devi
     const long mblocks = (M + k.bm - 1) / k.bm, nblocks = (N + k.bn - 1) / k.bn;
     const int kblocks = (K + 127) / 128;
     sc.tiles = mblocks * nblocks;
+    if (k.split > 1) {
+        // Split-K clusters: one cluster per tile, every tile at once (clusters beyond the
+        // resident ones start as earlier ones finish; no cluster waits on another).
+        sc.slots = std::max(1, dev.resident_ctas[config] / (k.ctas * k.split));
+        sc.dp_tiles = static_cast<int>(sc.tiles);
+        sc.grid = static_cast<int>(sc.tiles) * k.ctas * k.split;
+        return sc;
+    }
     sc.slots = std::max(1, dev.resident_ctas[config] / k.ctas);
     split_schedule(sc, kblocks, schedule);
     if (sc.sk_tiles > 0) {
@@ -362,14 +374,21 @@ Schedule make_schedule(int M, int N, int K, int config, int schedule, const Devi
 // Estimated relative time of a configuration under the data-parallel schedule: waves of
 // tiles over the resident slots times the per-SM share of one tile ((bm / ctas) x bn per
 // K block), divided by the configuration's measured relative efficiency.
-int choose_config(int M, int N, int K, const DeviceState& dev) {
+// Split-K cluster configurations take part only when `allow_split` (HGEMM_SCHEDULE_AUTO): an
+// explicit data-parallel or stream-K schedule keeps whole-K tiles, and with them the same
+// summation order, so the same bits, for any tile shape.
+int choose_config(int M, int N, int K, const DeviceState& dev, bool allow_split) {
     int best = 1;
     double best_cost = 1e300;
     for (int c = 1; c < kNumConfigs; ++c) {
         const KernelConfig& k = kConfigs[c];
         if (k.kbs > 1 && K % 128 != 0) continue;
         const Schedule sc = make_schedule(M, N, K, c, HGEMM_SCHEDULE_DATA_PARALLEL, dev);
-        const double area = static_cast<double>(k.bm / k.ctas) * k.bn;
+        // Split-K only where every cluster fits at once and each part keeps some depth.
+        // (Measured on B200: with fewer than 16 K blocks per part the exchange and the
+        // cluster start cost more than the split gains, e.g. 128 x 7168 x 2048.)
+        if (k.split > 1 && (!allow_split || sc.tiles > sc.slots || (K + 127) / 128 < 16 * k.split)) continue;
+        const double area = static_cast<double>(k.bm / k.ctas) * k.bn / k.split;
         const double work_per_slot = static_cast<double>((sc.tiles + sc.slots - 1) / sc.slots);
         const double cost = work_per_slot * area / k.eff;
         if (cost < best_cost - 1e-9) {
@@ -416,7 +435,7 @@ int run_gemm(const void* A, const void* B, void* C, int M, int N, int K, const f
         }
         return HGEMM_OK;
     }
-    const int c = config == 0 ? choose_config(M, N, K, *dev) : config;
+    const int c = config == 0 ? choose_config(M, N, K, *dev, schedule == HGEMM_SCHEDULE_AUTO) : config;
     const KernelConfig& kc = kConfigs[c];
     if (kc.kbs > 1 && K % 128 != 0) return HGEMM_ERR_UNSUPPORTED;  // (never chosen automatically then)
     const Schedule sc = make_schedule(M, N, K, c, schedule, *dev);
@@ -450,6 +469,7 @@ int run_gemm(const void* A, const void* B, void* C, int M, int N, int K, const f
     p.dp_tiles = sc.dp_tiles;
     p.sk_tiles = sc.sk_tiles;
     p.sk_slots = sc.sk_slots;
+    p.split_k = kc.split;
     p.debug_stall_first_stage = debug_stall;
     const SfMaps no_sf{};
     if (sc.sk_tiles == 0) return kc.launch(ta, tb, tc, p, peers, no_sf, sc.grid, stream);
@@ -604,7 +624,7 @@ int hgemm_workspace_bytes(int M, int N, int K, int config, int schedule, size_t*
     int rc = HGEMM_OK;
     const hg::DeviceState* dev = hg::current_device_setup(&rc);
     if (!dev) return rc;
-    const int c = config == 0 ? hg::choose_config(M, N, K, *dev) : config;
+    const int c = config == 0 ? hg::choose_config(M, N, K, *dev, schedule == HGEMM_SCHEDULE_AUTO) : config;
     const hg::Schedule sc = hg::make_schedule(M, N, K, c, schedule, *dev);
     *bytes_out = sc.sk_tiles > 0 ? sc.partial_bytes + sc.counter_bytes : 0;
     return HGEMM_OK;
@@ -618,7 +638,7 @@ int hgemm_plan(int M, int N, int K, int config, int schedule, int* plan_out) {
     int rc = HGEMM_OK;
     const hg::DeviceState* dev = hg::current_device_setup(&rc);
     if (!dev) return rc;
-    const int c = config == 0 ? hg::choose_config(M, N, K, *dev) : config;
+    const int c = config == 0 ? hg::choose_config(M, N, K, *dev, schedule == HGEMM_SCHEDULE_AUTO) : config;
     const hg::Schedule sc = hg::make_schedule(M, N, K, c, schedule, *dev);
     plan_out[0] = c;
     plan_out[1] = sc.grid;
@@ -639,6 +659,20 @@ int hgemm_debug_schedule(long long tiles, int slots, int kblocks, int schedule, 
     out3[1] = sc.sk_tiles;
     out3[2] = sc.sk_slots;
     return HGEMM_OK;
+}
+
+int hgemm_debug_split_work(int kblocks, int split, int tiles, int cta, int* out3) {
+    if (kblocks <= 0 || split < 2 || tiles <= 0 || cta < 0 || !out3) return HGEMM_ERR_INVALID_VALUE;
+    hg::GemmParams p{};
+    p.num_k_blocks = kblocks;
+    p.dp_tiles = tiles;
+    p.split_k = split;
+    hg::Work w;
+    if (!hg::get_work(p, cta, 0, 0, w)) return 0;
+    out3[0] = w.tile;
+    out3[1] = w.kb_begin;
+    out3[2] = w.kb_end;
+    return hg::get_work(p, cta, 0, 1, w) ? 2 : 1;  // a second item would be a bug
 }
 
 int hgemm_debug_work_items(int kblocks, int nslots, int dp_tiles, int sk_tiles, int sk_slots, int slot, int* out,
@@ -999,7 +1033,7 @@ extern "C" int hgemm_fp8_tn_static_scratch(const void* A, const void* B, void* C
     });
     if (st.status != HGEMM_OK) return st.status;
     if (K > 0) {
-        const int c = hg::choose_config(M, N, K, *dev);
+        const int c = hg::choose_config(M, N, K, *dev, false);
         const hg::Schedule sc = hg::make_schedule(M, N, K, c, HGEMM_SCHEDULE_STREAM_K, *dev);
         if (sc.partial_bytes + sc.counter_bytes > hg::kStaticScratchBytes) return HGEMM_ERR_UNSUPPORTED;
     }

@@ -153,6 +153,10 @@ int hgemm_fp8_tn_static_scratch(const void* A, const void* B, void* C, int M, in
 int hgemm_debug_schedule(long long tiles, int slots, int kblocks, int schedule, int* out3);
 int hgemm_debug_work_items(int kblocks, int nslots, int dp_tiles, int sk_tiles, int sk_slots, int slot, int* out,
                            int max_items);
+/* The split-K configurations' work: CTA `cta` of a grid of clusters of `split` CTAs over
+ * `tiles` tiles writes {tile, first K block, end K block}; returns the number of items the
+ * CTA gets (1; 0 past the last tile) or a negative status. */
+int hgemm_debug_split_work(int kblocks, int split, int tiles, int cta, int* out3);
 
 /* Number of tile configurations and their names ("bn256_s4" ...); NULL past the end. */
 int hgemm_num_configs(void);
@@ -162,7 +166,10 @@ const char* hgemm_config_name(int config);
 int hgemm_config_resident_ctas(int config);
 
 /* Synchronous.  Reads and clears the current device's kernel status word: 0 when no
- * bounded wait has expired since the last call, else the code of the first one. */
+ * bounded wait has expired since the last call, else the code of the first one,
+ * role << 8 | site: 0x0101 producer (stage free), 0x0201 / 0x0202 / 0x0203 MMA issuer
+ * (accumulator free, stage full, drain), 0x0301 epilogue (accumulator full), 0x0302 / 0x0303
+ * split-K epilogue (peers' buffers free, peers' partial rows in). */
 int hgemm_device_status(uint32_t* status_out);
 
 /* Human-readable text for an HGEMM_* status code (static storage). */

@@ -74,10 +74,41 @@ def test_ragged_tails(cuda_device, M, N, K):
     _run(M, N, K, seed_a=M, seed_b=N + K)
 
 
-@pytest.mark.parametrize("config", [1, 2, 3, 4, 5, 6])
+@pytest.mark.parametrize("config", [1, 2, 3, 4, 5, 6, 7, 8])
 @pytest.mark.parametrize("M,N,K", [(391, 648, 784), (1000, 1032, 2064), (2048, 2048, 1024)])
 def test_every_tile_config(cuda_device, config, M, N, K):
     _run(M, N, K, config=config)
+
+
+@pytest.mark.parametrize("config", ["bn128_s6_k2", "bn128_s6_k4"])
+@pytest.mark.parametrize("M,N,K", [(1, 8, 16), (7, 24, 48), (127, 136, 144), (129, 264, 272), (200, 520, 1040),
+                                   (128, 8288, 8192), (256, 4104, 4112), (64, 2240, 16400)])
+def test_split_k_clusters(cuda_device, config, M, N, K):
+    """Split-K over a cluster: each CTA's K part, summed in rank order through distributed
+    shared memory, matches the oracle, including K parts with no K block (K < 128 * ranks),
+    ragged M/N/K, and the skinny shape the configurations are for; repeated calls give the
+    same bits."""
+    import hipgemm_b200 as hg
+    c = hg.config_names().index(config)
+    A, B, sa, sb = make_inputs(M, N, K, seed_a=M + 1, seed_b=N + K)
+    a, b, ta, tb = to_device(A, B, sa, sb)
+    out = hg.fp8_gemm_tn(a, b, ta, tb, config=c)
+    again = hg.fp8_gemm_tn(a, b, ta, tb, config=c)
+    torch.cuda.synchronize()
+    assert hg.device_status() == 0
+    assert torch.equal(out.view(torch.int16), again.view(torch.int16))
+    rows = None if M * N * K <= 2**31 else sample_rows(M, 48)
+    bad, n, first = check_against_oracle(c_bits(out), A, B, sa, sb, rows=rows)
+    assert bad == 0, f"{bad}/{n} mismatches (first {first}) at {M}x{N}x{K} {config}"
+
+
+def test_split_k_chosen_for_skinny_shapes(cuda_device):
+    """The automatic choice takes a split-K cluster configuration where the tiles of a
+    128-row problem would leave most SMs idle, and not for large grids."""
+    import hipgemm_b200 as hg
+    split = {"bn128_s6_k2", "bn128_s6_k4"}
+    assert hg.plan(128, 8192, 8192)["config"] in split
+    assert hg.plan(8192, 8192, 8192)["config"] not in split
 
 
 def test_unscaled_and_one_scale(cuda_device):
@@ -151,7 +182,7 @@ def test_against_cublaslt_scaled_mm(cuda_device):
     assert oracle.validate(c_bits(lt), ref)[0] == 0
 
 
-@pytest.mark.parametrize("config", [1, 2, 3, 4, 5, 6])
+@pytest.mark.parametrize("config", [1, 2, 3, 4, 5, 6, 7, 8])
 @pytest.mark.parametrize("M,N,K", [(1000, 1032, 2064), (391, 648, 784), (128, 2048, 4096), (4000, 1024, 1152)])
 def test_stream_k_schedule(cuda_device, config, M, N, K):
     """Forced stream-K: partial tiles reduced by their last contributor match the oracle."""
@@ -197,7 +228,8 @@ def test_auto_plans(cuda_device):
     assert hg.plan(8192, 8192, 8192)["config"] == "pair256_s6"
     assert hg.plan(8192, 8192, 8192)["sk_tiles"] == 0
     assert hg.plan(128, 8192, 8192)["sk_tiles"] == 0  # automatic schedule: data-parallel
-    assert hg.plan(128, 8192, 8192, schedule=hg.HGEMM_SCHEDULE_STREAM_K)["sk_tiles"] > 0
+    bn128 = hg.config_names().index("bn128_s6")
+    assert hg.plan(128, 8192, 8192, config=bn128, schedule=hg.HGEMM_SCHEDULE_STREAM_K)["sk_tiles"] > 0
     assert hg.plan(1024, 8192, 8192, schedule=hg.HGEMM_SCHEDULE_STREAM_K)["sk_tiles"] > 0
     assert hg.plan(8192, 8192, 8192, schedule=hg.HGEMM_SCHEDULE_DATA_PARALLEL)["workspace_bytes"] == 0
 

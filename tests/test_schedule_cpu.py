@@ -82,3 +82,27 @@ def test_debug_entry_points_reject_bad_input():
     assert hg.lib().hgemm_debug_schedule(0, 74, 64, 0, out) == hg.HGEMM_ERR_INVALID_VALUE
     assert hg.lib().hgemm_debug_work_items(64, 74, 0, 10, 0, 0, out, 1) == hg.HGEMM_ERR_INVALID_VALUE
     assert hg.lib().hgemm_debug_work_items(64, 74, 0, 0, 0, 74, out, 1) == hg.HGEMM_ERR_INVALID_VALUE
+
+
+@pytest.mark.parametrize("split", [2, 4])
+@pytest.mark.parametrize("tiles,kblocks", [(37, 64), (74, 64), (1, 1), (3, 3), (5, 4), (2, 7), (37, 16), (9, 130)])
+def test_split_k_clusters_cover_every_unit_once(split, tiles, kblocks):
+    """The split-K configurations: CTA r of cluster t gets exactly K part r of tile t (one
+    item), the parts of a tile are contiguous, disjoint and cover all its K blocks in rank
+    order, and CTAs past the last cluster get nothing."""
+    L = hg.lib()
+    out = (ctypes.c_int * 3)()
+    for t in range(tiles):
+        parts = []
+        for r in range(split):
+            assert L.hgemm_debug_split_work(kblocks, split, tiles, t * split + r, out) == 1
+            assert out[0] == t
+            parts.append((out[1], out[2]))
+        assert parts[0][0] == 0 and parts[-1][1] == kblocks
+        for (b0, e0), (b1, e1) in zip(parts, parts[1:]):
+            assert e0 == b1 and b0 <= e0
+        # Balanced: part sizes differ by at most one K block.
+        sizes = [e - b for b, e in parts]
+        assert max(sizes) - min(sizes) <= 1
+    assert L.hgemm_debug_split_work(kblocks, split, tiles, tiles * split, out) == 0
+    assert L.hgemm_debug_split_work(kblocks, 1, tiles, 0, out) == hg.HGEMM_ERR_INVALID_VALUE

@@ -102,6 +102,27 @@ def test_split_k_clusters(cuda_device, config, M, N, K):
     assert bad == 0, f"{bad}/{n} mismatches (first {first}) at {M}x{N}x{K} {config}"
 
 
+def test_row_block_on_split_k(cuda_device):
+    """A 128-row block with long K (what one rank of a sharded skinny problem computes) takes
+    a split-K cluster configuration through hgemm_fp8_tn_rows: its rows match the oracle and
+    the rows outside the block are left untouched."""
+    import hipgemm_b200 as hg
+    M, N, K, r0, r1 = 384, 8192, 8192, 128, 256
+    assert hg.plan(r1 - r0, N, K)["config"] in {"bn128_s6_k2", "bn128_s6_k4"}
+    A, B, sa, sb = make_inputs(M, N, K, seed_a=5, seed_b=6)
+    a, b, ta, tb = to_device(A, B, sa, sb)
+    out = torch.full((M, N), 7.0, dtype=torch.bfloat16, device="cuda")
+    hg.fp8_gemm_tn_rows(a, b, out, r0, r1, ta, tb)
+    torch.cuda.synchronize()
+    assert hg.device_status() == 0
+    got = c_bits(out)
+    seven = np.uint16(0x40E0)  # bf16(7.0)
+    assert (got[:r0] == seven).all() and (got[r1:] == seven).all()
+    rows = r0 + sample_rows(r1 - r0, 24)
+    bad, n, first = check_against_oracle(got, A, B, sa, sb, rows=rows)
+    assert bad == 0, f"{bad}/{n} mismatches (first {first})"
+
+
 def test_split_k_chosen_for_skinny_shapes(cuda_device):
     """The automatic choice takes a split-K cluster configuration where the tiles of a
     128-row problem would leave most SMs idle, and not for large grids."""

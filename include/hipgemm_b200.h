@@ -101,8 +101,12 @@ int hgemm_fp8_tn_config(const void* A, const void* B, void* C, int M, int N, int
                         const float* d_scale_b, hgemm_stream_t stream, int config);
 
 /* Schedules for hgemm_fp8_tn_ex. */
-#define HGEMM_SCHEDULE_AUTO 0           /* the library's choice (currently data-parallel) */
-#define HGEMM_SCHEDULE_DATA_PARALLEL 1  /* whole output tiles only; needs no workspace */
+#define HGEMM_SCHEDULE_AUTO 0           /* the library's choice: data-parallel, or (automatic
+                                           configuration only) split-K over CTA clusters for
+                                           skinny problems with long K, whose bits differ from
+                                           the whole-K kernels' */
+#define HGEMM_SCHEDULE_DATA_PARALLEL 1  /* whole output tiles and whole K only, bits independent of
+                                           the tiling; needs no workspace */
 #define HGEMM_SCHEDULE_STREAM_K 2       /* split the last one-to-two waves of tiles along K across all
                                            SMs; partial tiles are reduced deterministically */
 

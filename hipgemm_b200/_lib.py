@@ -49,6 +49,7 @@ _SIGNATURES = {
     "hgemm_debug_schedule": (_i, [ctypes.c_longlong, _i, _i, _i, ctypes.POINTER(ctypes.c_int)]),
     "hgemm_debug_work_items": (_i, [_i, _i, _i, _i, _i, _i, ctypes.POINTER(ctypes.c_int), _i]),
     "hgemm_debug_split_work": (_i, [_i, _i, _i, _i, ctypes.POINTER(ctypes.c_int)]),
+    "hgemm_debug_choose": (_i, [_i, _i, _i, _i, ctypes.POINTER(ctypes.c_int), _i]),
     "hgemm_fp8_tn_rows_allgather": (_i, [_vp, _vp, ctypes.POINTER(ctypes.c_void_p), _i, _i, _i, _i, _i, _i, _i,
                                         _vp, _vp, _vp]),
     "hgemm_ipc_export": (_i, [_vp, _vp, ctypes.POINTER(ctypes.c_size_t)]),

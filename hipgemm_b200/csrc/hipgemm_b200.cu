@@ -345,7 +345,9 @@ void split_schedule(Schedule& sc, int kblocks, int schedule) {
     }
 }
 
-Schedule make_schedule(int M, int N, int K, int config, int schedule, const DeviceState& dev) {
+// resident_ctas[c]: CTAs of configuration c resident at once (DeviceState::resident_ctas; the
+// host-only test entry points pass their own).
+Schedule make_schedule(int M, int N, int K, int config, int schedule, const int* resident_ctas) {
     const KernelConfig& k = kConfigs[config];
     Schedule sc{};
     sc.config = config;
@@ -355,12 +357,12 @@ Schedule make_schedule(int M, int N, int K, int config, int schedule, const Devi
     if (k.split > 1) {
         // Split-K clusters: one cluster per tile, every tile at once (clusters beyond the
         // resident ones start as earlier ones finish; no cluster waits on another).
-        sc.slots = std::max(1, dev.resident_ctas[config] / (k.ctas * k.split));
+        sc.slots = std::max(1, resident_ctas[config] / (k.ctas * k.split));
         sc.dp_tiles = static_cast<int>(sc.tiles);
         sc.grid = static_cast<int>(sc.tiles) * k.ctas * k.split;
         return sc;
     }
-    sc.slots = std::max(1, dev.resident_ctas[config] / k.ctas);
+    sc.slots = std::max(1, resident_ctas[config] / k.ctas);
     split_schedule(sc, kblocks, schedule);
     if (sc.sk_tiles > 0) {
         sc.partial_bytes = align_up(static_cast<size_t>(sc.sk_slots) * 2 * k.ctas * k.partial_floats * 4, 256);
@@ -371,19 +373,23 @@ Schedule make_schedule(int M, int N, int K, int config, int schedule, const Devi
     return sc;
 }
 
+Schedule make_schedule(int M, int N, int K, int config, int schedule, const DeviceState& dev) {
+    return make_schedule(M, N, K, config, schedule, dev.resident_ctas);
+}
+
 // Estimated relative time of a configuration under the data-parallel schedule: waves of
 // tiles over the resident slots times the per-SM share of one tile ((bm / ctas) x bn per
 // K block), divided by the configuration's measured relative efficiency.
 // Split-K cluster configurations take part only when `allow_split` (HGEMM_SCHEDULE_AUTO): an
 // explicit data-parallel or stream-K schedule keeps whole-K tiles, and with them the same
 // summation order, so the same bits, for any tile shape.
-int choose_config(int M, int N, int K, const DeviceState& dev, bool allow_split) {
+int choose_config(int M, int N, int K, const int* resident_ctas, bool allow_split) {
     int best = 1;
     double best_cost = 1e300;
     for (int c = 1; c < kNumConfigs; ++c) {
         const KernelConfig& k = kConfigs[c];
         if (k.kbs > 1 && K % 128 != 0) continue;
-        const Schedule sc = make_schedule(M, N, K, c, HGEMM_SCHEDULE_DATA_PARALLEL, dev);
+        const Schedule sc = make_schedule(M, N, K, c, HGEMM_SCHEDULE_DATA_PARALLEL, resident_ctas);
         // Split-K only where every cluster fits at once and each part keeps some depth.
         // (Measured on B200: with fewer than 16 K blocks per part the exchange and the
         // cluster start cost more than the split gains, e.g. 128 x 7168 x 2048.)
@@ -397,6 +403,10 @@ int choose_config(int M, int N, int K, const DeviceState& dev, bool allow_split)
         }
     }
     return best;
+}
+
+int choose_config(int M, int N, int K, const DeviceState& dev, bool allow_split) {
+    return choose_config(M, N, K, dev.resident_ctas, allow_split);
 }
 
 bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
@@ -659,6 +669,15 @@ int hgemm_debug_schedule(long long tiles, int slots, int kblocks, int schedule, 
     out3[1] = sc.sk_tiles;
     out3[2] = sc.sk_slots;
     return HGEMM_OK;
+}
+
+int hgemm_debug_choose(int M, int N, int K, int schedule, const int* resident_ctas, int n_configs) {
+    if (M <= 0 || N <= 0 || K <= 0 || !resident_ctas || n_configs != hg::kNumConfigs) return HGEMM_ERR_INVALID_VALUE;
+    if (schedule < HGEMM_SCHEDULE_AUTO || schedule > HGEMM_SCHEDULE_STREAM_K) return HGEMM_ERR_INVALID_VALUE;
+    for (int c = 1; c < n_configs; ++c) {
+        if (resident_ctas[c] <= 0) return HGEMM_ERR_INVALID_VALUE;
+    }
+    return hg::choose_config(M, N, K, resident_ctas, schedule == HGEMM_SCHEDULE_AUTO);
 }
 
 int hgemm_debug_split_work(int kblocks, int split, int tiles, int cta, int* out3) {

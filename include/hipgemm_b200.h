@@ -161,6 +161,11 @@ int hgemm_debug_work_items(int kblocks, int nslots, int dp_tiles, int sk_tiles, 
  * `tiles` tiles writes {tile, first K block, end K block}; returns the number of items the
  * CTA gets (1; 0 past the last tile) or a negative status. */
 int hgemm_debug_split_work(int kblocks, int split, int tiles, int cta, int* out3);
+/* The automatic configuration choice, on the host, for a device that keeps resident_ctas[c]
+ * CTAs of configuration c resident at once (n_configs = hgemm_num_configs(); entry 0 unused):
+ * what hgemm_fp8_tn with `schedule` would run.  Returns the configuration index or a
+ * negative status. */
+int hgemm_debug_choose(int M, int N, int K, int schedule, const int* resident_ctas, int n_configs);
 
 /* Number of tile configurations and their names ("bn256_s4" ...); NULL past the end. */
 int hgemm_num_configs(void);

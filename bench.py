@@ -47,7 +47,28 @@ METRIC = "FP8 e4m3 GEMM TFLOP/s and % of dense FP8 peak"
 # the same workload (see profiles/); keyed by (workload, gpus).  None = not captured.
 TRAFFIC_BYTES_PER_LAUNCH: dict[tuple[str, int], float] = {
     ("8192", 1): 345.692e6 + 117.302e6,  # profiles/fp8_gemm_tn_8192_pair256.md (<2, 256, 6>, current build)
+    ("skinny128", 1): 68.216e6 + 1.242e6,  # profiles/fp8_gemm_tn_128x8192x8192_splitk2.md (split-K, 2-CTA clusters)
 }
+
+
+def roofline(flops: float, alg_bytes: float, ms: float, tensor_peak: tuple[float, str],
+             tensor_peak_sustained: float | None, hbm_peak: tuple[float, str], traffic: float | None) -> dict:
+    """The bound of one launch from its arithmetic intensity: below the ridge (dense FP8 peak ÷
+    HBM bandwidth) it is HBM-bound and `achieved` is algorithmic GB/s against the measured HBM
+    peak; above it, TFLOP/s against the dense FP8 peak (with the sustained fraction beside)."""
+    ridge = tensor_peak[0] * 1e12 / (hbm_peak[0] * 1e9)
+    if flops / alg_bytes < ridge:
+        gbs = alg_bytes / (ms * 1e-3) / 1e9
+        return {"bound": "hbm", "achieved": gbs, "peak": hbm_peak[0], "unit": "GB/s", "frac": gbs / hbm_peak[0],
+                "traffic": traffic, "peak_source": hbm_peak[1], "algorithmic_bytes": alg_bytes,
+                "arithmetic_intensity": flops / alg_bytes, "ridge": ridge}
+    tf = flops / (ms * 1e-3) / 1e12
+    return {"bound": "tensor", "achieved": tf, "peak": tensor_peak[0], "unit": "TFLOP/s", "frac": tf / tensor_peak[0],
+            "traffic": traffic, "peak_source": tensor_peak[1],
+            # The timed loop runs at the power-capped clock (ncu cycles / event time ~1.3 GHz),
+            # the regime of the sustained figure; `frac` keeps the burst one.
+            "peak_sustained": tensor_peak_sustained,
+            "frac_sustained": tf / tensor_peak_sustained if tensor_peak_sustained else None}
 
 
 def parse_args():
@@ -444,7 +465,6 @@ def run_ours(args) -> None:
     value = flops_total / (ms * 1e-3) / 1e12
     peak, peak_src = fp8_peak_tflops()
     peak_sus = fp8_peak_sustained_tflops()
-    achieved = flops_rank / (ms * 1e-3) / 1e12  # one launch per step on this rank
     traffic = TRAFFIC_BYTES_PER_LAUNCH.get((args.workload, world))
 
     extra = {}
@@ -540,13 +560,9 @@ def run_ours(args) -> None:
                        "l2": f"rotating inputs: {nbuf} (A,B) sets = {nbuf * set_bytes / 2**20:.0f} MiB per GPU "
                              f"> 126 MB L2"},
             "pct_dense_fp8_peak": 100.0 * value / (world * peak),
-            "roofline": {"bound": "tensor", "achieved": achieved, "peak": peak, "unit": "TFLOP/s",
-                         "frac": achieved / peak, "traffic": traffic, "peak_source": peak_src,
-                         "kernel": "hg::fp8_gemm_tn_sm100 (per-GPU launch, CUDA events on its stream)",
-                         # The timed loop runs at the power-capped clock (ncu cycles / event time
-                         # ~1.3 GHz), the regime of the sustained figure; `frac` keeps the burst one.
-                         "peak_sustained": peak_sus,
-                         "frac_sustained": achieved / peak_sus if peak_sus else None},
+            "roofline": dict(roofline(flops_rank, float(m * K + N * K + 2 * m * N), ms, (peak, peak_src), peak_sus,
+                                      hbm_peak, traffic),
+                             kernel="hg::fp8_gemm_tn_sm100 (per-GPU launch, CUDA events on its stream)"),
             "cpu_baseline": cpu,
             "e2e": e2e,
             "gpu_launches": args.steps,

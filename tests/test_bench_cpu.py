@@ -1,0 +1,35 @@
+"""bench.py's roofline arithmetic (no GPU): a launch is tensor-bound or HBM-bound by its
+arithmetic intensity against the ridge (dense FP8 peak / HBM bandwidth), and `achieved` is
+the algorithmic rate in that bound's unit."""
+import math
+
+import bench
+
+PEAK = (3236.8, "measured")  # TFLOP/s, dense FP8 (2 x the driver's bf16 figure)
+HBM = (6549.4, "measured")   # GB/s
+
+
+def test_headline_is_tensor_bound():
+    M = N = K = 8192
+    flops, alg = 2.0 * M * N * K, float(M * K + N * K + 2 * M * N)
+    r = bench.roofline(flops, alg, 0.38, PEAK, 2759.6, HBM, 463e6)
+    assert r["bound"] == "tensor" and r["unit"] == "TFLOP/s"
+    assert math.isclose(r["achieved"], flops / 0.38e-3 / 1e12)
+    assert math.isclose(r["frac"], r["achieved"] / PEAK[0])
+    assert math.isclose(r["frac_sustained"], r["achieved"] / 2759.6)
+    assert r["traffic"] == 463e6
+
+
+def test_skinny_is_hbm_bound():
+    M, N, K = 128, 8192, 8192
+    flops, alg = 2.0 * M * N * K, float(M * K + N * K + 2 * M * N)
+    r = bench.roofline(flops, alg, 0.0186, PEAK, 2759.6, HBM, None)
+    assert r["bound"] == "hbm" and r["unit"] == "GB/s"
+    assert math.isclose(r["achieved"], alg / 0.0186e-3 / 1e9)  # ~3780 GB/s
+    assert math.isclose(r["frac"], r["achieved"] / HBM[0])
+    assert r["arithmetic_intensity"] < r["ridge"]
+
+
+def test_traffic_table_names_real_workloads():
+    for (workload, world), traffic in bench.TRAFFIC_BYTES_PER_LAUNCH.items():
+        assert workload in bench.WORKLOADS and world >= 1 and traffic > 0

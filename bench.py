@@ -8,8 +8,8 @@ One step = one GEMM launch over one batch (one rotating (A, B) pair) of the work
 at N > 1 (launched by torchrun) rows of M are split across the ranks and B is
 replicated (hipgemm_b200/shard.py), so total work is fixed ("strong" scaling).
 Timing follows the reference's bench.cpp:16-115 (rotating input buffers to defeat the
-cache, warm-up, CUDA events) with the contract's rules: W warm-up steps, exactly K
-timed steps bracketed by a barrier and a device synchronize, max over ranks.
+cache, warm-up, CUDA events), with W warm-up steps, exactly K timed steps bracketed by
+a barrier and a device synchronize, and the max over ranks.
 
 --impl reference times the reference's own CPU GEMM (test.cpp:19-30, restated in
 oracle/ because the reference needs ROCm + an MI355X) on this machine's host cores.
@@ -44,7 +44,7 @@ L2_BYTES = 126 * 2**20
 METRIC = "FP8 e4m3 GEMM TFLOP/s and % of dense FP8 peak"
 
 # DRAM bytes (read + write) of one launch of the GEMM kernel, from an ncu capture of
-# the same workload (see profiles/); keyed by (workload, gpus).  None = not captured.
+# the same workload; keyed by (workload, gpus).  None = not captured.
 TRAFFIC_BYTES_PER_LAUNCH: dict[tuple[str, int], float] = {
     # ncu dram__bytes_read.sum + dram__bytes_write.sum of one launch of the automatic choice:
     ("8192", 1): 345.692e6 + 117.302e6,    # fp8_gemm_tn_sm100<2, 256, 6> at 8192^3

@@ -37,6 +37,11 @@
 // would use, so there is one accumulator and the epilogue releases it as soon as the tile is
 // drained (EARLY_RELEASE).
 //
+// SPLIT > 1 is split-K over a cluster of SPLIT single CTAs, for problems whose tiles would
+// leave most SMs idle (a 128-row M with long K): CTA r of a cluster computes K part r of the
+// cluster's tile, and the CTAs exchange partial rows through distributed shared memory (bulk
+// copies into each other's idle stage rings) so that each finishes 128 / SPLIT rows.
+//
 // CTA-pair synchronisation uses no multicast form: tcgen05.commit always targets a
 // barrier of the even CTA, and the even CTA forwards each completion to its peer with a
 // remote mbarrier.arrive that the peer acquires at cluster scope:

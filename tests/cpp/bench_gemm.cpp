@@ -1,0 +1,153 @@
+// Benchmark harness in the style of the reference's bench.cpp (nirw4nna/hipgemm bench.cpp:16-115),
+// calling the B200 kernel through the C ABI.  Same flow: rotating device buffers (together at
+// least 512 MiB of A or of B, so consecutive launches do not find their operands in L2), each
+// filled from pinned host memory with the seeded generator (utils.hpp:27-33; seeds 2i and 2i+1),
+// warm-up launches, then timed launches with events around each one and C cleared before it,
+// and the best and average times as TFLOP/s.  Unscaled e4m3 inputs, as in the reference.
+//
+//   ./bench_gemm                      compile-time MDIM x NDIM x KDIM (default 8192^3), launched
+//                                     through the drop-in fp8_gemm_4wave_256x256x128<M, N, K>
+//   ./bench_gemm W I                  the same with W warm-up and I timed launches
+//   ./bench_gemm W I M N K            runtime shape through hgemm_fp8_tn
+//
+// Differences from the reference: the iteration counts are arguments (the reference fixes 1000
+// and 1000), and every library status and the kernel status word are checked.
+#include <cuda_runtime.h>
+
+#include <algorithm>
+#include <cstdio>
+#include <cstdlib>
+#include <vector>
+
+#include "hipgemm_b200.h"
+
+#ifndef MDIM
+#define MDIM 8192
+#endif
+#ifndef NDIM
+#define NDIM 8192
+#endif
+#ifndef KDIM
+#define KDIM 8192
+#endif
+
+#define CHECK_CUDA(expr)                                                                           \
+    do {                                                                                           \
+        cudaError_t e_ = (expr);                                                                   \
+        if (e_ != cudaSuccess) {                                                                   \
+            fprintf(stderr, "CUDA error: '%s'(%d) at %s:%d\n", cudaGetErrorString(e_), int(e_),   \
+                    __FILE__, __LINE__);                                                           \
+            exit(EXIT_FAILURE);                                                                    \
+        }                                                                                          \
+    } while (0)
+
+#define CHECK_HGEMM(expr)                                                                          \
+    do {                                                                                           \
+        int rc_ = (expr);                                                                          \
+        if (rc_ != HGEMM_OK) {                                                                     \
+            fprintf(stderr, "hgemm error: %s (%d) at %s:%d\n", hgemm_error_string(rc_), rc_,      \
+                    __FILE__, __LINE__);                                                           \
+            exit(EXIT_FAILURE);                                                                    \
+        }                                                                                          \
+    } while (0)
+
+int main(int argc, char** argv) {
+    const int warmup_iters = argc >= 3 ? std::atoi(argv[1]) : 1000;
+    const int iters = argc >= 3 ? std::atoi(argv[2]) : 1000;
+    const bool runtime_shape = argc >= 6;
+    const int M = runtime_shape ? std::atoi(argv[3]) : MDIM;
+    const int N = runtime_shape ? std::atoi(argv[4]) : NDIM;
+    const int K = runtime_shape ? std::atoi(argv[5]) : KDIM;
+    if (warmup_iters < 0 || iters < 1 || M < 1 || N < 1 || K < 1) {
+        fprintf(stderr, "usage: %s [warmup iters [M N K]]\n", argv[0]);
+        return EXIT_FAILURE;
+    }
+
+    const size_t a_bytes = size_t(M) * K, b_bytes = size_t(N) * K, c_bytes = size_t(M) * N * 2;
+    // Enough rotating (A, B) sets that all of A's, or all of B's, span at least 512 MiB.
+    const size_t span = size_t(512) << 20;
+    const size_t nbuf = std::max<size_t>(1, std::max(span / (2 * a_bytes), span / (2 * b_bytes)));
+
+    uint8_t* A_host = nullptr;
+    uint8_t* B_host = nullptr;
+    CHECK_CUDA(cudaMallocHost(&A_host, a_bytes));
+    CHECK_CUDA(cudaMallocHost(&B_host, b_bytes));
+    uint8_t* A_dev = nullptr;
+    uint8_t* B_dev = nullptr;
+    void* C_dev = nullptr;
+    CHECK_CUDA(cudaMalloc(&A_dev, nbuf * a_bytes));
+    CHECK_CUDA(cudaMalloc(&B_dev, nbuf * b_bytes));
+    CHECK_CUDA(cudaMalloc(&C_dev, c_bytes));
+
+    printf("%s, %d x %d x %d\n", hgemm_version(), M, N, K);
+    printf("Initializing %zu rotating buffer blocks\n", nbuf);
+    for (size_t i = 0; i < nbuf; ++i) {
+        hgemm_host_init_random(A_host, a_bytes, 2 * i, -1.0f, 1.0f);
+        hgemm_host_init_random(B_host, b_bytes, 2 * i + 1, -1.0f, 1.0f);
+        CHECK_CUDA(cudaMemcpy(A_dev + i * a_bytes, A_host, a_bytes, cudaMemcpyHostToDevice));
+        CHECK_CUDA(cudaMemcpy(B_dev + i * b_bytes, B_host, b_bytes, cudaMemcpyHostToDevice));
+    }
+    printf("Buffer initialization finished\n");
+
+    // One launch on the legacy default stream, with A and B from rotating set `set`.
+    auto launch = [&](size_t set) {
+        const uint8_t* A = A_dev + set * a_bytes;
+        const uint8_t* B = B_dev + set * b_bytes;
+        if (runtime_shape) {
+            CHECK_HGEMM(hgemm_fp8_tn(A, B, C_dev, M, N, K, nullptr, nullptr, nullptr));
+        } else {
+            CHECK_HGEMM((fp8_gemm_4wave_256x256x128<MDIM, NDIM, KDIM>(A, B, C_dev)));
+        }
+    };
+
+    printf("\n%d warmup iterations...\n", warmup_iters);
+    for (int i = 0; i < warmup_iters; ++i) {
+        CHECK_CUDA(cudaMemsetAsync(C_dev, 0, c_bytes, nullptr));
+        launch(size_t(i) % nbuf);
+        CHECK_CUDA(cudaDeviceSynchronize());
+    }
+
+    cudaEvent_t start, stop;
+    CHECK_CUDA(cudaEventCreate(&start));
+    CHECK_CUDA(cudaEventCreate(&stop));
+    std::vector<float> times_ms;
+    times_ms.reserve(iters);
+    printf("%d benchmark iterations...\n", iters);
+    for (int i = 0; i < iters; ++i) {
+        CHECK_CUDA(cudaMemsetAsync(C_dev, 0, c_bytes, nullptr));
+        CHECK_CUDA(cudaEventRecord(start, nullptr));
+        launch(size_t(i + warmup_iters) % nbuf);
+        CHECK_CUDA(cudaEventRecord(stop, nullptr));
+        CHECK_CUDA(cudaEventSynchronize(stop));
+        float ms = 0.0f;
+        CHECK_CUDA(cudaEventElapsedTime(&ms, start, stop));
+        times_ms.push_back(ms);
+    }
+    uint32_t status = 0;
+    const int st = hgemm_device_status(&status);
+    if (st != HGEMM_OK) {
+        fprintf(stderr, "kernel status word %#x: a bounded wait expired (%s)\n", status, hgemm_error_string(st));
+        return EXIT_FAILURE;
+    }
+
+    double sum_ms = 0.0;
+    float best_ms = times_ms[0];
+    for (float t : times_ms) {
+        sum_ms += t;
+        best_ms = std::min(best_ms, t);
+    }
+    const double avg_ms = sum_ms / double(times_ms.size());
+    const double flop = 2.0 * double(M) * double(N) * double(K);
+    printf("\n=== PERFORMANCE RESULTS ===\n");
+    printf("  Kernel time (best): %.5f ms,  TFLOPS: %.2f\n", best_ms, flop / (best_ms * 1e-3) / 1e12);
+    printf("  Kernel time (avg ): %.5f ms,  TFLOPS: %.2f\n", avg_ms, flop / (avg_ms * 1e-3) / 1e12);
+
+    CHECK_CUDA(cudaEventDestroy(start));
+    CHECK_CUDA(cudaEventDestroy(stop));
+    CHECK_CUDA(cudaFreeHost(A_host));
+    CHECK_CUDA(cudaFreeHost(B_host));
+    CHECK_CUDA(cudaFree(A_dev));
+    CHECK_CUDA(cudaFree(B_dev));
+    CHECK_CUDA(cudaFree(C_dev));
+    return EXIT_SUCCESS;
+}

@@ -272,7 +272,8 @@ def fp8_gemm_tn_mx(a: torch.Tensor, b: torch.Tensor, sfa_blocked: torch.Tensor, 
     """OCP MX e4m3 GEMM (one e8m0 scale per 32 K elements of each row of a and b, blocked
     layout from mx_sf_to_blocked, on the device): C = sa*sb * sum_k (a 2^sfa)(b 2^sfb).
     config: 0 chooses by wave count, 1 = 128 x 256 tiles, 2 = 128 x 128 tiles, 3 = 256 x 256
-    tiles on CTA pairs."""
+    tiles on CTA pairs; 4 and 5 = configs 3 and 2 with two K blocks per TMA load (K % 128 == 0,
+    else HgemmError)."""
     _check_operand("a", a)
     _check_operand("b", b)
     M, K = a.shape

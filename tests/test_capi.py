@@ -81,6 +81,44 @@ def test_python_wrapper_refuses_cpu_tensors():
         hg.fp8_gemm_tn(torch.zeros((8, 16), dtype=torch.float32), a)
 
 
+def test_every_device_entry_point_refuses_cpu_tensors():
+    """There is no CPU path: each torch-facing entry point raises before any CUDA call when
+    handed host tensors (or host tensors where device buffers belong)."""
+    import torch
+    a = torch.zeros((8, 64), dtype=torch.uint8)
+    x = torch.zeros((8, 64), dtype=torch.float32)
+    sf = torch.zeros(hg.lib().hgemm_mx_sf_bytes(8, 64), dtype=torch.uint8)
+    out = torch.empty((8, 8), dtype=torch.bfloat16)
+    with pytest.raises(ValueError, match="CUDA"):
+        hg.fp8_gemm_tn_rows(a, a, out, 0, 8)
+    with pytest.raises(ValueError, match="CUDA"):
+        hg.fp8_gemm_tn_mx(a, a, sf, sf)
+    with pytest.raises(ValueError, match="CUDA"):
+        hg.quantize_e4m3(x)
+    with pytest.raises(ValueError, match="CUDA"):
+        hg.quantize_e4m3_delayed(x, torch.ones(1))
+    with pytest.raises(ValueError, match="CUDA"):
+        hg.quantize_mx_e4m3(x)
+    with pytest.raises(TypeError):
+        hg.fp8_gemm_tn_mx(x, a, sf, sf)  # fp32 is not an e4m3 operand
+
+
+def test_host_helpers_check_their_arguments():
+    import torch
+    a = torch.zeros((8, 64), dtype=torch.uint8)
+    c = torch.empty((8, 8), dtype=torch.bfloat16)
+    with pytest.raises(ValueError, match="c_host"):
+        hg.fp8_gemm_tn_from_host(a, a, torch.empty((8, 9), dtype=torch.bfloat16), None, a, a, c)
+    with pytest.raises(ValueError, match="d_c"):
+        hg.fp8_gemm_tn_from_host(a, a, c, None, a, a, torch.empty((8, 9), dtype=torch.bfloat16))
+    with pytest.raises(ValueError, match="scales_host"):
+        hg.fp8_gemm_tn_from_host(a, a, c, torch.ones(3), a, a, c)
+    with pytest.raises(ValueError, match="sf"):
+        hg.mx_sf_to_blocked(torch.zeros((8, 2), dtype=torch.float32), 64)
+    with pytest.raises(ValueError, match="sf"):
+        hg.mx_sf_to_blocked(torch.zeros((8, 3), dtype=torch.uint8), 64)  # K/32 columns expected
+
+
 def test_header_compiles_as_cpp_and_c(tmp_path):
     cpp = tmp_path / "use.cpp"
     cpp.write_text(

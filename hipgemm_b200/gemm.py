@@ -82,9 +82,11 @@ def fp8_gemm_tn(a: torch.Tensor, b: torch.Tensor, scale_a: torch.Tensor | None =
                 stream: torch.cuda.Stream | None = None) -> torch.Tensor:
     """C[M,N] (bf16) = scale_a * scale_b * a[M,K] @ b[N,K]^T, fp32 accumulation.
 
-    config: tile configuration (0 = automatic, see config_names()); schedule: 0 automatic,
-    1 data-parallel only, 2 stream-K; workspace: optional caller-owned device buffer for a
-    stream-K schedule (else the library's stream-ordered pool is used)."""
+    config: tile configuration (0 = automatic, see config_names()); schedule: 0 automatic
+    (may pick split-K over CTA clusters for skinny problems with long K: reproducible bits, but
+    not those of the whole-K kernels), 1 data-parallel only (whole-K tiles: the same bits for
+    any tiling), 2 stream-K; workspace: optional caller-owned device buffer for a stream-K
+    schedule (else the library's stream-ordered pool is used)."""
     _check_operand("a", a)
     _check_operand("b", b)
     M, K = a.shape

@@ -70,6 +70,8 @@ _SIGNATURES = {
     "hgemm_config_resident_ctas": (_i, [_i]),
     "hgemm_config_name": (ctypes.c_char_p, [_i]),
     "hgemm_device_status": (_i, [ctypes.POINTER(ctypes.c_uint32)]),
+    "hgemm_debug_workspace_pool_created": (_i, [_i]),
+    "hgemm_fp8_tn_static_scratch": (_i, [_vp, _vp, _vp, _i, _i, _i, _vp, _vp, _vp]),
     "hgemm_error_string": (ctypes.c_char_p, [_i]),
     "hgemm_version": (ctypes.c_char_p, []),
     "hgemm_host_init_random": (None, [_vp, ctypes.c_size_t, ctypes.c_uint64, ctypes.c_float, ctypes.c_float]),

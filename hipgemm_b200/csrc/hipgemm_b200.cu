@@ -36,7 +36,11 @@ struct DeviceState {
     // num_sms / 2 (clusters must fit inside one GPC).
     int resident_ctas[kMaxConfigs] = {};
     int mx_resident_ctas[kMaxConfigs] = {};  // the same for the MX configurations
-    cudaMemPool_t pool = nullptr;  // stream-K workspaces
+    // Stream-K workspaces: a library-owned stream-ordered pool, created by the first call that
+    // needs library-allocated scratch (never by device_setup, so that entry points with their
+    // own scratch never create one).
+    std::mutex pool_mutex;
+    cudaMemPool_t pool = nullptr;
 };
 
 DeviceState g_devices[kMaxDevices];
@@ -224,22 +228,32 @@ int device_setup(int dev) {
                 return;
             }
         }
-        // Library-owned stream-ordered pool for stream-K workspaces; it keeps its memory
-        // (release threshold = max) so repeated calls do not map pages again.
-        cudaMemPoolProps props{};
-        props.allocType = cudaMemAllocationTypePinned;
-        props.location.type = cudaMemLocationTypeDevice;
-        props.location.id = dev;
-        if (cudaMemPoolCreate(&st.pool, &props) != cudaSuccess) {
-            st.status = HGEMM_ERR_CUDA;
-            return;
-        }
-        uint64_t threshold = UINT64_MAX;
-        cudaMemPoolSetAttribute(st.pool, cudaMemPoolAttrReleaseThreshold, &threshold);
         st.num_sms = prop.multiProcessorCount;
         st.status = HGEMM_OK;
     });
     return st.status;
+}
+
+// The device's stream-K workspace pool, created on first use.  It keeps its memory (release
+// threshold = max) so repeated calls do not map pages again.  A failed creation is not
+// cached: the next call tries again.
+cudaMemPool_t workspace_pool(int dev) {
+    DeviceState& st = g_devices[dev];
+    std::lock_guard<std::mutex> lock(st.pool_mutex);
+    if (st.pool) return st.pool;
+    cudaMemPoolProps props{};
+    props.allocType = cudaMemAllocationTypePinned;
+    props.location.type = cudaMemLocationTypeDevice;
+    props.location.id = dev;
+    cudaMemPool_t pool = nullptr;
+    if (cudaMemPoolCreate(&pool, &props) != cudaSuccess) {
+        cudaGetLastError();
+        return nullptr;
+    }
+    uint64_t threshold = UINT64_MAX;
+    cudaMemPoolSetAttribute(pool, cudaMemPoolAttrReleaseThreshold, &threshold);
+    st.pool = pool;
+    return pool;
 }
 
 const DeviceState* current_device_setup(int* rc) {
@@ -488,9 +502,13 @@ int run_gemm(const void* A, const void* B, void* C, int M, int N, int K, const f
     void* ws = workspace;
     if (ws) {
         if (workspace_bytes < need || (reinterpret_cast<uintptr_t>(ws) & 255u)) return HGEMM_ERR_INVALID_VALUE;
-    } else if (cudaMallocFromPoolAsync(&ws, need, dev->pool, stream) != cudaSuccess) {
-        cudaGetLastError();
-        return HGEMM_ERR_CUDA;
+    } else {
+        const cudaMemPool_t pool = workspace_pool(static_cast<int>(dev - g_devices));
+        if (!pool) return HGEMM_ERR_CUDA;
+        if (cudaMallocFromPoolAsync(&ws, need, pool, stream) != cudaSuccess) {
+            cudaGetLastError();
+            return HGEMM_ERR_CUDA;
+        }
     }
     p.partials = static_cast<float*>(ws);
     p.counters = reinterpret_cast<int*>(static_cast<uint8_t*>(ws) + sc.partial_bytes);
@@ -937,6 +955,13 @@ const char* hgemm_config_name(int config) {
     return hg::kConfigs[config].name;
 }
 
+int hgemm_debug_workspace_pool_created(int device) {
+    if (device < 0 || device >= hg::kMaxDevices) return HGEMM_ERR_INVALID_VALUE;
+    hg::DeviceState& st = hg::g_devices[device];
+    std::lock_guard<std::mutex> lock(st.pool_mutex);
+    return st.pool ? 1 : 0;
+}
+
 int hgemm_device_status(uint32_t* status_out) {
     uint32_t v = 0;
     if (cudaMemcpyFromSymbol(&v, hg::g_status, sizeof(v)) != cudaSuccess) return HGEMM_ERR_CUDA;
@@ -1018,11 +1043,26 @@ constexpr size_t kStaticScratchBytes = static_cast<size_t>(8) << 20;
 static __device__ __align__(256) uint8_t g_static_scratch[kStaticScratchBytes];
 
 struct StaticScratch {
-    std::once_flag once;
-    void* ptr = nullptr;  // device address of g_static_scratch on this device
-    int status = HGEMM_ERR_CUDA;
+    std::mutex mutex;
+    void* ptr = nullptr;  // device address of g_static_scratch on this device, once looked up
 };
 StaticScratch g_static_scratch_ptrs[kMaxDevices];
+
+// The array's device address on device `d` (current), looked up on the first call that
+// succeeds; a failed lookup is not cached, so a later call retries it.
+void* static_scratch_address(int d) {
+    StaticScratch& st = g_static_scratch_ptrs[d];
+    std::lock_guard<std::mutex> lock(st.mutex);
+    if (!st.ptr) {
+        void* p = nullptr;
+        if (cudaGetSymbolAddress(&p, g_static_scratch) == cudaSuccess && p) {
+            st.ptr = p;
+        } else {
+            cudaGetLastError();
+        }
+    }
+    return st.ptr;
+}
 
 }  // namespace
 }  // namespace hg
@@ -1040,24 +1080,16 @@ extern "C" int hgemm_fp8_tn_static_scratch(const void* A, const void* B, void* C
     }
     // In host code g_static_scratch names a host-side stand-in, not device memory: the
     // device address comes from cudaGetSymbolAddress, once per device, with it current.
-    hg::StaticScratch& st = hg::g_static_scratch_ptrs[d];
-    std::call_once(st.once, [&]() {
-        void* p = nullptr;
-        if (cudaGetSymbolAddress(&p, hg::g_static_scratch) == cudaSuccess && p) {
-            st.ptr = p;
-            st.status = HGEMM_OK;
-        } else {
-            cudaGetLastError();
-        }
-    });
-    if (st.status != HGEMM_OK) return st.status;
+    void* const scratch = hg::static_scratch_address(d);
+    if (!scratch) return HGEMM_ERR_CUDA;
     if (K > 0) {
         const int c = hg::choose_config(M, N, K, *dev, false);
         const hg::Schedule sc = hg::make_schedule(M, N, K, c, HGEMM_SCHEDULE_STREAM_K, *dev);
         if (sc.partial_bytes + sc.counter_bytes > hg::kStaticScratchBytes) return HGEMM_ERR_UNSUPPORTED;
     }
     // run_gemm zeroes the tile counters in the scratch (cudaMemsetAsync on `stream`) before
-    // the launch; the partial tiles are always written before they are read.
+    // the launch; the partial tiles are always written before they are read.  With a
+    // workspace given, run_gemm never touches the library's workspace pool.
     return hg::run_gemm(A, B, C, M, N, K, d_scale_a, d_scale_b, reinterpret_cast<cudaStream_t>(stream), 0,
-                        HGEMM_SCHEDULE_STREAM_K, st.ptr, hg::kStaticScratchBytes);
+                        HGEMM_SCHEDULE_STREAM_K, scratch, hg::kStaticScratchBytes);
 }

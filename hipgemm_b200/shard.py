@@ -135,10 +135,17 @@ def stream_barrier(group=None) -> None:
 
 
 def run_allgather(sg: ShardedGemm, a_rows: torch.Tensor, b: torch.Tensor, bufs: PeerCBuffers, scale_a=None,
-                  scale_b=None, barrier: bool = True) -> torch.Tensor:
+                  scale_b=None, barrier: bool = True, barrier_before: bool = True) -> torch.Tensor:
     """This rank's rows of C = A . B^T computed and written into every rank's full C in
-    one kernel (hgemm_fp8_tn_rows_allgather); with barrier=True, a stream barrier
-    follows so that bufs.local holds the whole C for work queued after this call."""
+    one kernel (hgemm_fp8_tn_rows_allgather).
+
+    The kernel writes into every peer's buffer, so two stream barriers bracket it:
+    barrier_before=True orders it after every rank's work queued before this call (in
+    particular any reads of the previous result: without it, this rank's stores could
+    overwrite a peer's C while that peer is still reading it), and barrier=True orders every
+    rank's stores before work queued after this call, so that bufs.local holds the whole C.
+    Leave barrier_before on unless the caller orders its reads of the buffers against the
+    next call some other way."""
     _check_operand("a_rows", a_rows)
     _check_operand("b", b)
     if tuple(a_rows.shape) != (sg.rows, sg.K) or tuple(b.shape) != (sg.N, sg.K):
@@ -148,6 +155,8 @@ def run_allgather(sg: ShardedGemm, a_rows: torch.Tensor, b: torch.Tensor, bufs: 
     # a_rows holds rows [row_begin, row_end): pass its pointer as the base of rows
     # [0, rows) of a virtual full A, i.e. shift by -row_begin rows.
     a_base = a_rows.data_ptr() - sg.row_begin * sg.K
+    if barrier_before:
+        stream_barrier(sg.group)
     with torch.cuda.device(a_rows.device):
         rc = lib().hgemm_fp8_tn_rows_allgather(a_base, _ptr(b), bufs.ptrs, sg.world, sg.rank, sg.M, sg.N, sg.K,
                                                sg.row_begin, sg.row_end, _ptr(scale_a), _ptr(scale_b),

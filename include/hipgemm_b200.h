@@ -114,8 +114,10 @@ int hgemm_fp8_tn_config(const void* A, const void* B, void* C, int M, int N, int
  * caller-owned device workspace (256-byte aligned, at least hgemm_workspace_bytes(); its
  * content on entry does not matter).  With workspace == NULL a stream-K schedule takes
  * its workspace from a library-owned stream-ordered pool (cudaMallocFromPoolAsync /
- * cudaFreeAsync on `stream`).  Calls that share a caller workspace must not overlap on
- * the GPU.  No counterpart in the reference, whose launch shape is fixed. */
+ * cudaFreeAsync on `stream`), which the first such call on a device creates
+ * (cudaMemPoolCreate); make that first call before any stream capture.  Calls that share
+ * a caller workspace must not overlap on the GPU.  No counterpart in the reference, whose
+ * launch shape is fixed. */
 int hgemm_fp8_tn_ex(const void* A, const void* B, void* C, int M, int N, int K, const float* d_scale_a,
                     const float* d_scale_b, hgemm_stream_t stream, int config, int schedule, void* workspace,
                     size_t workspace_bytes);
@@ -136,15 +138,18 @@ int hgemm_plan(int M, int N, int K, int config, int schedule, int* plan_out);
  * needs no scratch.  Same arguments and result contract as hgemm_fp8_tn; it runs the
  * HGEMM_SCHEDULE_STREAM_K schedule with its scratch in a fixed 8 MiB device array inside
  * this library (held by every GPU that loads the library until the process exits) and
- * calls no cudaMalloc, cudaFree or other allocating routine.
+ * calls no cudaMalloc, cudaFree, memory-pool or other allocating routine, on its first
+ * call too: the library's workspace pool is never created on this path.
  * Limit: a problem whose stream-K scratch exceeds 8 MiB (see hgemm_workspace_bytes with
  * HGEMM_SCHEDULE_STREAM_K) is refused with HGEMM_ERR_UNSUPPORTED before anything is
  * launched; the data-parallel schedule (hgemm_fp8_tn_ex, HGEMM_SCHEDULE_DATA_PARALLEL)
  * needs no scratch for any size.
- * The first call on a device also looks up the array's device address; make that first
- * call before any stream capture.  Every call shares the one array and finds the last
- * call's contents in it (this entry point clears what must start at zero), so calls that
- * overlap on the GPU, from any stream or thread, race: serialise them. */
+ * The first call on a device runs the library's one-time device set-up (device properties,
+ * kernel attributes, occupancy queries) and looks up the array's device address; make that
+ * first call before any stream capture.  A failed lookup is retried by the next call.
+ * Every call shares the one array and finds the last call's contents in it (this entry
+ * point clears what must start at zero), so calls that overlap on the GPU, from any stream
+ * or thread, race: serialise them. */
 int hgemm_fp8_tn_static_scratch(const void* A, const void* B, void* C, int M, int N, int K, const float* d_scale_a,
                                 const float* d_scale_b, hgemm_stream_t stream);
 
@@ -180,6 +185,11 @@ int hgemm_config_resident_ctas(int config);
  * (accumulator free, stage full, drain), 0x0301 epilogue (accumulator full), 0x0302 / 0x0303
  * split-K epilogue (peers' buffers free, peers' partial rows in). */
 int hgemm_device_status(uint32_t* status_out);
+
+/* Test hook: 1 if the library's stream-K workspace pool exists on `device` (it is created
+ * by the first hgemm_fp8_tn_ex call there that needs library-allocated scratch), 0 if not,
+ * HGEMM_ERR_INVALID_VALUE for a bad index.  Makes no CUDA call. */
+int hgemm_debug_workspace_pool_created(int device);
 
 /* Human-readable text for an HGEMM_* status code (static storage). */
 const char* hgemm_error_string(int code);

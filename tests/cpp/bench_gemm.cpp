@@ -1,6 +1,6 @@
 // Benchmark harness in the style of the reference's bench.cpp (nirw4nna/hipgemm bench.cpp:16-115),
 // calling the B200 kernel through the C ABI.  Same flow: rotating device buffers (together at
-// least 512 MiB of A or of B, so consecutive launches do not find their operands in L2), each
+// least 512 MiB, at least two sets, at most 1 GiB unless two sets need more), each
 // filled from pinned host memory with the seeded generator (utils.hpp:27-33; seeds 2i and 2i+1),
 // warm-up launches, then timed launches with events around each one and C cleared before it,
 // and the best and average times as TFLOP/s.  Unscaled e4m3 inputs, as in the reference.
@@ -64,9 +64,13 @@ int main(int argc, char** argv) {
     }
 
     const size_t a_bytes = size_t(M) * K, b_bytes = size_t(N) * K, c_bytes = size_t(M) * N * 2;
-    // Enough rotating (A, B) sets that all of A's, or all of B's, span at least 512 MiB.
-    const size_t span = size_t(512) << 20;
-    const size_t nbuf = std::max<size_t>(1, std::max(span / (2 * a_bytes), span / (2 * b_bytes)));
+    // Rotating (A, B) sets: enough that together they span at least 512 MiB (four times the
+    // 126 MB L2, so consecutive launches do not find their operands there), at least two, and
+    // no more than fit in 1 GiB (the reference sizes by one operand, bench.cpp:24, which asks
+    // for 16 GiB of B at 128 x 8192 x 8192).
+    const size_t set_bytes = a_bytes + b_bytes;
+    const size_t span = size_t(512) << 20, budget = size_t(1) << 30;
+    const size_t nbuf = std::max<size_t>(2, std::min((span + set_bytes - 1) / set_bytes, budget / set_bytes));
 
     uint8_t* A_host = nullptr;
     uint8_t* B_host = nullptr;

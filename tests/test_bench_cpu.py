@@ -33,3 +33,26 @@ def test_skinny_is_hbm_bound():
 def test_traffic_table_names_real_workloads():
     for (workload, world), traffic in bench.TRAFFIC_BYTES_PER_LAUNCH.items():
         assert workload in bench.WORKLOADS and world >= 1 and traffic > 0
+
+
+def test_parity_rows_cover_every_rank_edge_and_row_block():
+    from hipgemm_b200.shard import row_range
+    for M, world in [(8192, 1), (8192, 8), (16384, 4), (1000, 3), (128, 2)]:
+        rows = bench.parity_rows(M, world)
+        assert rows == sorted(set(rows)) and 0 <= rows[0] and rows[-1] < M
+        for r in range(world):
+            r0, r1 = row_range(M, r, world)
+            assert r0 in rows and r1 - 1 in rows
+        blocks = {x // 128 for x in rows}
+        assert blocks == set(range((M + 127) // 128))
+
+
+def test_both_arms_report_the_same_config():
+    """The reference arm and ours describe the workload with the same dict."""
+    import inspect
+    src = inspect.getsource(bench.run_reference) + inspect.getsource(bench.run_ours)
+    assert src.count('"config": workload_config(args.workload)') == 2
+    for name in bench.WORKLOADS:
+        c = bench.workload_config(name)
+        M, N, K, _ = bench.WORKLOADS[name]
+        assert (c["M"], c["N"], c["K"]) == (M, N, K) and "l2" in c

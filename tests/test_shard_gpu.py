@@ -88,7 +88,8 @@ def _fused_worker(rank, world, port, M, N, K, out_dir):
         ok = True
         for step in range(2):  # twice: the buffers are rewritten in place
             bufs.local.fill_(float("nan"))
-            stream_barrier()  # nobody writes into a buffer before its owner has cleared it
+            # run_allgather's barrier_before: nobody writes into a buffer before its owner
+            # has cleared it (and, in a real loop, finished reading the previous result).
             full = run_allgather(sg, a, b, bufs, ta, tb)
             torch.cuda.synchronize()
             ok = ok and torch.equal(full.view(torch.int16), single.view(torch.int16))

@@ -156,10 +156,11 @@ __host__ __device__ __forceinline__ bool get_work(const GemmParams& p, int slot,
     const int KB = p.num_k_blocks;
     if (p.split_k > 1) {
         if (idx > 0) return false;
+        // 32-bit arithmetic: KB < 2^24 and split_k <= 4 (a 64-bit divide is a long subroutine).
         const int part = slot % p.split_k;
         w.tile = slot / p.split_k;
-        w.kb_begin = static_cast<int>(static_cast<long long>(part) * KB / p.split_k);
-        w.kb_end = static_cast<int>(static_cast<long long>(part + 1) * KB / p.split_k);
+        w.kb_begin = part * KB / p.split_k;
+        w.kb_end = (part + 1) * KB / p.split_k;
         w.piece = 2;
         return w.tile < p.dp_tiles;
     }
@@ -368,7 +369,15 @@ __global__ void __launch_bounds__(192, 1)
     volatile uint32_t* const abort_flag = reinterpret_cast<volatile uint32_t*>(smem_gen + S::OFF_MISC + 4);
     volatile int* const bcast = reinterpret_cast<volatile int*>(smem_gen + S::OFF_MISC + 8);
 
-    if (threadIdx.x == 0) {
+    const int slot = static_cast<int>(blockIdx.x) / CTAS;
+    const int nslots = static_cast<int>(gridDim.x) / CTAS;
+
+    // Set-up, spread over three warps.  On an SM that has not run this code yet, the first
+    // pass through it and the first reads of the kernel parameters cost about a microsecond
+    // of instruction and constant fetches; the producer spends that time working out its first
+    // work item while another warp initialises the barriers, so its first copies go out as
+    // soon as griddep_wait returns.
+    if (warp == 2 && lane == 0) {
         for (int s = 0; s < STAGES; ++s) {
             mbar_init(bar_full + 8 * s, 1);
             mbar_init(bar_empty + 8 * s, 1);
@@ -385,6 +394,11 @@ __global__ void __launch_bounds__(192, 1)
         *abort_flag = 0u;
         fence_mbarrier_init();
         fence_proxy_async_smem();
+    }
+    Work w_first{};
+    bool have_first = false;
+    int mb_first = 0, nb_first = 0;
+    if (warp == 0 && lane == 0) {
         prefetch_tmap(&tm_a);
         prefetch_tmap(&tm_b);
         prefetch_tmap(&tm_c);
@@ -392,8 +406,12 @@ __global__ void __launch_bounds__(192, 1)
             prefetch_tmap(&sfm.a);
             prefetch_tmap(&sfm.b);
         }
+        have_first = get_work(p, slot, nslots, 0, w_first);
+        if (have_first) tile_coords(w_first.tile, p, mb_first, nb_first);
     }
     if (warp == 1) {
+        // The MMA issuer's first work item, for the same reason as the producer's.
+        if (lane == 0) have_first = get_work(p, slot, nslots, 0, w_first);
         tmem_alloc<CTAS>(tmem_slot, S::TMEM_COLS);  // for a pair: collective with the peer's warp 1
         tmem_relinquish<CTAS>();
     }
@@ -410,9 +428,6 @@ __global__ void __launch_bounds__(192, 1)
     griddep_launch_dependents();
     griddep_wait();
 
-    const int slot = static_cast<int>(blockIdx.x) / CTAS;
-    const int nslots = static_cast<int>(gridDim.x) / CTAS;
-
     if (warp == 0) {
         // ---------------- TMA producer (one thread per CTA) ----------------
         if (lane == 0) {
@@ -422,10 +437,11 @@ __global__ void __launch_bounds__(192, 1)
             uint32_t phase = 0;
             bool first_pass = true;
             bool ok = true;
-            Work w;
-            for (int idx = 0; ok && get_work(p, slot, nslots, idx, w); ++idx) {
-                int mb, nb;
-                tile_coords(w.tile, p, mb, nb);
+            Work w = w_first;
+            bool have = have_first;
+            for (int idx = 0; ok && have; ++idx, have = get_work(p, slot, nslots, idx, w)) {
+                int mb = mb_first, nb = nb_first;
+                if (idx > 0) tile_coords(w.tile, p, mb, nb);
                 const int a_row = mb * S::BM + static_cast<int>(rank) * 128;
                 const int b_row = nb * BN + static_cast<int>(rank) * S::B_ROWS;
                 for (int kb = w.kb_begin; kb < w.kb_end; kb += KBS) {
@@ -506,8 +522,9 @@ __global__ void __launch_bounds__(192, 1)
                     tmem_cp_32x128b_warpx4<CTAS>(tsfa + 4 * (1 + c), sf_smem_desc(sf_src + 512 * (KBS * (1 + c) + h)));
                 }
             };
-            Work w;
-            for (int idx = 0; ok && get_work(p, slot, nslots, idx, w); ++idx) {
+            Work w = w_first;
+            bool have = have_first;
+            for (int idx = 0; ok && have; ++idx, have = get_work(p, slot, nslots, idx, w)) {
                 if (!mbar_wait<kPair>(bar_tempty + 8 * acc, acc_phase ^ 1u, abort_flag, kErrMmaTmemEmpty)) {
                     ok = false;
                     break;
@@ -861,17 +878,31 @@ __global__ void __launch_bounds__(192, 1)
                 continue;
             }
             if (w.piece < 0) {
-#pragma unroll 1
-                for (int c = 0; c < BN / EC; ++c) {
-                    uint32_t r[EC];
+                // The tensor-memory loads of chunk c + 1 are in flight while chunk c is scaled,
+                // rounded and stored, and the accumulator is released as soon as its last chunk
+                // is in registers (before that chunk's store).
+                constexpr int NCH = BN / EC;
+                uint32_t ra[EC], rb[EC];
+                auto load_chunk = [&](int c, uint32_t (&r)[EC]) {
 #pragma unroll
                     for (int h = 0; h < EC / 32; ++h) {
                         tmem_ld_32x32b_x32(tmem_row + c * EC + 32 * h, *reinterpret_cast<uint32_t(*)[32]>(&r[32 * h]));
                     }
-                    tmem_ld_wait();
-                    store_chunk(*reinterpret_cast<const float(*)[EC]>(&r[0]), row0, nb * BN + c * EC);
+                };
+                load_chunk(0, ra);
+#pragma unroll
+                for (int c = 0; c < NCH; ++c) {
+                    uint32_t(&cur)[EC] = (c & 1) ? rb : ra;
+                    uint32_t(&nxt)[EC] = (c & 1) ? ra : rb;
+                    tmem_ld_wait(*reinterpret_cast<uint32_t(*)[32]>(&cur[0]));
+                    if constexpr (EC == 64) reg_fence(*reinterpret_cast<uint32_t(*)[32]>(&cur[32]));
+                    if (c + 1 < NCH) {
+                        load_chunk(c + 1, nxt);
+                    } else {
+                        release_accumulator();
+                    }
+                    store_chunk(*reinterpret_cast<const float(*)[EC]>(&cur[0]), row0, nb * BN + c * EC);
                 }
-                release_accumulator();
                 continue;
             }
 

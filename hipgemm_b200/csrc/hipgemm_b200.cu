@@ -25,6 +25,13 @@ using EncodeTiledFn = CUresult (*)(CUtensorMap*, CUtensorMapDataType, cuuint32_t
 
 constexpr int kMaxDevices = 64;
 
+// Tile rows per raster group (measured best for pairs too: 8192^3 2948 against 2874 TFLOP/s
+// with 8).  HG_GROUP_M overrides it at build time for sweeps.
+#ifndef HG_GROUP_M
+#define HG_GROUP_M 16
+#endif
+constexpr int kGroupM = HG_GROUP_M;
+
 constexpr int kMaxConfigs = 16;
 
 struct DeviceState {
@@ -487,7 +494,7 @@ int run_gemm(const void* A, const void* B, void* C, int M, int N, int K, const f
     p.num_m_blocks = (M + kc.bm - 1) / kc.bm;
     p.num_n_blocks = (N + kc.bn - 1) / kc.bn;
     p.num_k_blocks = (K + 127) / 128;
-    p.group_m = 16;  // measured best for pairs too (8192^3: 2948 vs 2874 TFLOP/s at 8)
+    p.group_m = kGroupM;
     p.scale_a = sa;
     p.scale_b = sb;
     p.dp_tiles = sc.dp_tiles;
@@ -550,7 +557,7 @@ int run_gemm_mx(const void* A, const void* B, void* C, int M, int N, int K, cons
     p.num_m_blocks = (M + kc.bm - 1) / kc.bm;
     p.num_n_blocks = (N + kc.bn - 1) / kc.bn;
     p.num_k_blocks = (K + 127) / 128;
-    p.group_m = 16;
+    p.group_m = kGroupM;
     p.scale_a = sa;
     p.scale_b = sb;
     p.dp_tiles = p.num_m_blocks * p.num_n_blocks;

@@ -106,6 +106,9 @@ constexpr int kSfRowsPerAtom = 4;
 constexpr int kMaxPeerOutputs = 7;
 struct PeerOutputs {
     CUtensorMap maps[kMaxPeerOutputs];
+    // The same outputs as C stores of 128-row boxes (one CTA's rows at once): wide[0] is this
+    // GPU's C, wide[1 + i] peer i's.  Whole data-parallel tiles are stored through these.
+    CUtensorMap wide[kMaxPeerOutputs + 1];
     int count;
 };
 
@@ -131,6 +134,10 @@ __host__ __device__ __forceinline__ void tile_coords(int tile, const GemmParams&
     const int r = tile - group * per_group;
     mb = first_m + r % rows_in_group;
     nb = r / rows_in_group;
+    // Odd groups walk the columns backwards, so a group starts on the B panels its
+    // predecessor used last, still in L2 (measured at 8192^3: DRAM reads 238 -> 227 MB per
+    // launch; 16384 x 28672 x 8192: 1455 -> 1423 MB).
+    if (group & 1) nb = p.num_n_blocks - 1 - nb;
 }
 
 struct Work {
@@ -402,6 +409,7 @@ __global__ void __launch_bounds__(192, 1)
         prefetch_tmap(&tm_a);
         prefetch_tmap(&tm_b);
         prefetch_tmap(&tm_c);
+        prefetch_tmap(&peers.wide[0]);
         if constexpr (MX) {
             prefetch_tmap(&sfm.a);
             prefetch_tmap(&sfm.b);
@@ -636,6 +644,39 @@ __global__ void __launch_bounds__(192, 1)
                 bulk_commit_group();  // an empty group when the store was skipped keeps the count exact
             }
             ++chunk_ctr;
+        };
+
+        // CTA-wide stores (whole data-parallel tiles): the four epilogue warps stage one
+        // EC-column chunk of all 128 rows of this CTA, then a single thread issues one 128-row
+        // TMA store.  Issuing a TMA store costs its thread ~150 ns (measured), a quarter of what
+        // four 32-row stores per chunk cost; the issuing thread rotates over the warps' lane 0s.
+        // Buffers alternate per chunk; a thread that issued a store waits for it to have read
+        // shared memory before the next chunk's barrier, so that the buffer is free when chunk
+        // c + 2 is staged into it.
+        const uint32_t wide_base = base + S::OFF_EPI;
+        uint32_t wide_ctr = 0;
+        auto store_wide = [&](const uint32_t* packed, int cta_row0, int col0) {
+            const uint32_t buf = wide_base + (wide_ctr & 1u) * 4u * S::EPI_BUF_BYTES;
+            const uint32_t row_addr = buf + quad * S::EPI_BUF_BYTES + lane * (EC * 2u);
+#pragma unroll
+            for (int q = 0; q < EC / 8; ++q) {
+                // The swizzle of row 32 quad + lane, whose row % 8 is lane % 8.
+                const uint32_t slot16 = EC == 64 ? (static_cast<uint32_t>(q) ^ (lane & 7u))
+                                                 : (static_cast<uint32_t>(q) ^ ((lane >> 1) & 3u));
+                st_shared_v4(row_addr + slot16 * 16u, packed[4 * q], packed[4 * q + 1], packed[4 * q + 2],
+                             packed[4 * q + 3]);
+            }
+            fence_proxy_async_smem();
+            if (lane == 0) bulk_wait_group_read<0>();  // this thread's last store has read its buffer
+            named_bar_sync(2, 128);
+            if (lane == 0 && (wide_ctr & 3u) == epi_idx) {
+                if (cta_row0 < p.M && col0 < p.N) {
+                    tma_store_2d(&peers.wide[0], col0, cta_row0, buf);
+                    for (int i = 0; i < peers.count; ++i) tma_store_2d(&peers.wide[1 + i], col0, cta_row0, buf);
+                }
+                bulk_commit_group();
+            }
+            ++wide_ctr;
         };
 
         // Scale EC fp32 accumulators of this thread's row, round to bf16 (RNE) and store.
@@ -882,6 +923,14 @@ __global__ void __launch_bounds__(192, 1)
                 // rounded and stored, and the accumulator is released as soon as its last chunk
                 // is in registers (before that chunk's store).
                 constexpr int NCH = BN / EC;
+                const int cta_row0 = mb * S::BM + static_cast<int>(rank) * 128;
+                // With a stream-K schedule, partial tiles store through the per-warp buffers,
+                // which overlap the CTA-wide ones: every earlier store must have read its buffer
+                // before this tile stages into them.
+                if (p.sk_tiles > 0) {
+                    if (lane == 0) bulk_wait_group_read<0>();
+                    named_bar_sync(2, 128);
+                }
                 uint32_t ra[EC], rb[EC];
                 auto load_chunk = [&](int c, uint32_t (&r)[EC]) {
 #pragma unroll
@@ -901,7 +950,17 @@ __global__ void __launch_bounds__(192, 1)
                     } else {
                         release_accumulator();
                     }
-                    store_chunk(*reinterpret_cast<const float(*)[EC]>(&cur[0]), row0, nb * BN + c * EC);
+                    uint32_t packed[EC / 2];
+#pragma unroll
+                    for (int j = 0; j < EC / 2; ++j) {
+                        packed[j] = pack_bf16x2_rn(__fmul_rn(__uint_as_float(cur[2 * j]), s),
+                                                   __fmul_rn(__uint_as_float(cur[2 * j + 1]), s));
+                    }
+                    store_wide(packed, cta_row0, nb * BN + c * EC);
+                }
+                if (p.sk_tiles > 0) {
+                    if (lane == 0) bulk_wait_group_read<0>();
+                    named_bar_sync(2, 128);
                 }
                 continue;
             }

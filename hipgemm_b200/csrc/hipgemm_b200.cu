@@ -480,9 +480,17 @@ int run_gemm(const void* A, const void* B, void* C, int M, int N, int K, const f
     }
     PeerOutputs peers{};
     if (n_peer < 0 || n_peer > kMaxPeerOutputs) return HGEMM_ERR_INVALID_VALUE;
+    // 128-row boxes for the CTA-wide stores of whole tiles (wide[0] = C).
+    if (!encode_2d(&peers.wide[0], CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, C, static_cast<uint64_t>(N),
+                   static_cast<uint64_t>(M), static_cast<uint32_t>(kc.epi_cols), 128, c_swizzle,
+                   static_cast<uint64_t>(ldc) * 2)) {
+        return HGEMM_ERR_CUDA;
+    }
     for (int i = 0; i < n_peer; ++i) {
         if (!encode_2d(&peers.maps[i], CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, peer_c[i], static_cast<uint64_t>(N),
-                       static_cast<uint64_t>(M), static_cast<uint32_t>(kc.epi_cols), 32, c_swizzle)) {
+                       static_cast<uint64_t>(M), static_cast<uint32_t>(kc.epi_cols), 32, c_swizzle) ||
+            !encode_2d(&peers.wide[1 + i], CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, peer_c[i], static_cast<uint64_t>(N),
+                       static_cast<uint64_t>(M), static_cast<uint32_t>(kc.epi_cols), 128, c_swizzle)) {
             return HGEMM_ERR_CUDA;
         }
     }
@@ -571,7 +579,12 @@ int run_gemm_mx(const void* A, const void* B, void* C, int M, int N, int K, cons
                       static_cast<uint32_t>(kc.bn / 128), kc.kbs)) {
         return HGEMM_ERR_CUDA;
     }
-    const PeerOutputs peers{};
+    PeerOutputs peers{};
+    if (!encode_2d(&peers.wide[0], CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, C, static_cast<uint64_t>(N),
+                   static_cast<uint64_t>(M), static_cast<uint32_t>(kc.epi_cols), 128,
+                   kc.epi_cols == 64 ? CU_TENSOR_MAP_SWIZZLE_128B : CU_TENSOR_MAP_SWIZZLE_64B)) {
+        return HGEMM_ERR_CUDA;
+    }
     const int slots = dev->mx_resident_ctas[ci] / kc.ctas;
     const int grid = kc.ctas * std::min(p.dp_tiles, slots);
     return kc.launch(ta, tb, tc, p, peers, sfm, grid, stream);

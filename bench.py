@@ -62,9 +62,10 @@ def workload_config(name: str) -> dict:
 # DRAM bytes (read + write) of one launch of the GEMM kernel, from an ncu capture of
 # the same workload; keyed by (workload, gpus).  None = not captured.
 TRAFFIC_BYTES_PER_LAUNCH: dict[tuple[str, int], float] = {
-    # ncu dram__bytes_read.sum + dram__bytes_write.sum of one launch of the automatic choice:
-    ("8192", 1): 345.692e6 + 117.302e6,    # fp8_gemm_tn_sm100<2, 256, 6> at 8192^3
-    ("skinny128", 1): 68.216e6 + 1.242e6,  # fp8_gemm_tn_sm100<1, 128, 6, 0, 1, 2> (split-K) at 128 x 8192 x 8192
+    # ncu dram__bytes_read.sum + dram__bytes_write.sum of one launch of the automatic choice
+    # (profiles/fp8_gemm_tn_8192_pair256.md, profiles/fp8_gemm_tn_128x8192x8192_splitk2.md):
+    ("8192", 1): 232.149e6 + 117.133e6,    # fp8_gemm_tn_sm100<2, 256, 6> at 8192^3
+    ("skinny128", 1): 68.223e6 + 1.460e6,  # fp8_gemm_tn_sm100<1, 128, 6, 0, 1, 2> (split-K) at 128 x 8192 x 8192
 }
 
 

@@ -656,6 +656,21 @@ def run_ours(args) -> None:
     if status != 0:
         raise SystemExit(f"kernel status word {status:#x}: a bounded wait expired")
 
+    extra = {}
+    # The check of the timed run's last result, right after the timed region (outside it, and
+    # before any other leg writes C).
+    bufs = None
+    if world > 1 and not args.no_allgather:
+        from hipgemm_b200.shard import PeerCBuffers
+        bufs = PeerCBuffers(M, N, dev)
+    if not args.no_parity:
+        extra["parity"] = parity_check(hg, sg, A[last_set], B[last_set], SA[last_set], SB[last_set], C, dev, world,
+                                       rank, bufs)
+        torch.cuda.synchronize()
+        barrier()
+        if hg.device_status() != 0:
+            raise SystemExit("kernel status word set during the parity check: a bounded wait expired")
+
     flops_total = 2.0 * M * N * K
     flops_rank = 2.0 * m * N * K
     value = flops_total / (ms * 1e-3) / 1e12
@@ -663,7 +678,6 @@ def run_ours(args) -> None:
     peak_sus = fp8_peak_sustained_tflops()
     traffic = TRAFFIC_BYTES_PER_LAUNCH.get((args.workload, world))
 
-    extra = {}
     if not args.no_cublas:
         def lt_step(i):
             j = i % nbuf
@@ -719,19 +733,6 @@ def run_ours(args) -> None:
     e2e = {"value": flops_total / (ms_e2e * 1e-3) / 1e12, "unit": "TFLOP/s", "api": "hgemm_fp8_tn_from_host",
            "h2d_bytes_per_step": int(hA.numel() + hB.numel() + 4 * hS.numel()),
            "d2h_bytes_per_step": int(2 * hC.numel()), "steps": e2e_steps, "ms_per_step": ms_e2e}
-
-    # The post-run check of the timed run's last result (outside every timed region).
-    bufs = None
-    if world > 1 and not args.no_allgather:
-        from hipgemm_b200.shard import PeerCBuffers
-        bufs = PeerCBuffers(M, N, dev)
-    if not args.no_parity:
-        extra["parity"] = parity_check(hg, sg, A[last_set], B[last_set], SA[last_set], SB[last_set], C, dev, world,
-                                       rank, bufs)
-        torch.cuda.synchronize()
-        barrier()
-        if hg.device_status() != 0:
-            raise SystemExit("kernel status word set during the parity check: a bounded wait expired")
 
     if bufs is not None:
         from hipgemm_b200.shard import run_allgather

@@ -119,8 +119,7 @@ enum : uint32_t {
     kErrMmaFull = 0x0202,
     kErrMmaDrain = 0x0203,
     kErrEpiTmemFull = 0x0301,
-    kErrSplitFree = 0x0302,  // split-K: a peer's receive buffer never became free
-    kErrSplitFull = 0x0303,  // split-K: the peers' partial rows never all arrived
+    kErrSplitFull = 0x0303,  // split-K: the peers' partial columns never all arrived
 };
 
 // Output tile -> (m block, n block) with GROUP_M tile rows per raster group: inside a
@@ -284,8 +283,8 @@ struct KernelShape {
     // pair's CTAs both hold all of B's), column block major: two loads per stage.
     static constexpr int SFB_ATOMS = (BN + 127) / 128;
     static constexpr int SF_BYTES = MX ? 512 * (1 + SFB_ATOMS) * KBS : 0;
-    // full, empty, tfull x2, tempty x2, drain (+ split-K: receive buffer free, partials in)
-    static constexpr int NUM_BARS = 2 * STAGES + 5 + (SPLIT > 1 ? 2 : 0);
+    // full, empty, tfull x2, tempty x2, drain (+ split-K: peers' partials in)
+    static constexpr int NUM_BARS = 2 * STAGES + 5 + (SPLIT > 1 ? 1 : 0);
     // bf16 columns per staged epilogue chunk: 64 (128-byte rows, 128-byte swizzle) when
     // BN allows and the staging fits beside the stage ring, else 32 (64-byte rows, 64-byte
     // swizzle; also the one-accumulator MX tile, to fit four stages).
@@ -296,7 +295,8 @@ struct KernelShape {
     static constexpr int OFF_A = 0;
     static constexpr int OFF_B = OFF_A + STAGES * A_BYTES;
     static constexpr int OFF_EPI = OFF_B + STAGES * B_BYTES;
-    static constexpr int OFF_SF = OFF_EPI + 4 * 2 * EPI_BUF_BYTES;
+    static constexpr int OFF_RECV = OFF_EPI + 4 * 2 * EPI_BUF_BYTES;  // split-K receive region
+    static constexpr int OFF_SF = OFF_RECV + (SPLIT > 1 ? (SPLIT - 1) * 4 * (BN / SPLIT / 32) * 4096 : 0);
     static constexpr int OFF_BAR = OFF_SF + STAGES * SF_BYTES;
     static constexpr int OFF_MISC = OFF_BAR + NUM_BARS * 8;
     static constexpr int SMEM_BYTES = OFF_MISC + 16 + 1024;  // + slack to align the base to 1024 B
@@ -320,25 +320,25 @@ struct KernelShape {
     static_assert(CTAS == 1 || BN % 16 == 0, "M=256 MMAs need N % 16 == 0");
     static_assert(KB_B_BYTES % 1024 == 0, "B tiles must keep 1024-byte alignment");
     static_assert(KBS == 1 || KBS == 2, "one or two K blocks per stage");
-    // Split-K: each CTA of the cluster finishes SPLIT_ROWS rows of the tile (SPLIT_QUADS
-    // epilogue warps' worth).  Its stage ring, idle once its MMAs are done, holds
-    //   [0, RECV_BYTES): the peers' fp32 partials of those rows, one 32-row block
-    //       (WARP_BLOCK_BYTES) per (peer, row group), peers in rank order without itself;
-    //   [RECV_BYTES, + RECV_BYTES): its own partial rows for the other ranks, staged by the
-    //       warps that hold them and sent with one bulk copy per warp.
-    // A block is column-chunk major (chunk c of 32 columns at 4096 c, 128 bytes per row); inside
-    // a chunk, row r's 16-byte unit u sits at unit u ^ (r & 7): eight lanes (rows) touching the
-    // same unit hit eight different bank groups.
-    static constexpr int SPLIT_ROWS = 128 / SPLIT;
-    static constexpr int SPLIT_QUADS = SPLIT_ROWS / 32;
-    static constexpr int WARP_BLOCK_BYTES = 32 * BN * 4;
-    static constexpr int RECV_BYTES = SPLIT > 1 ? (SPLIT - 1) * SPLIT_QUADS * WARP_BLOCK_BYTES : 0;
+    // Split-K: each CTA of the cluster finishes OWN_COLS columns of the tile (all 128 rows, so
+    // all four epilogue warps share the work).  As soon as its own MMAs are done, each warp
+    // stages its 32 rows of every other rank's columns in its (now idle) stage ring and sends
+    // them with one bulk copy per owner into the owner's dedicated receive region:
+    //   [RECV_OFF, + RECV_BYTES): one SLOT_BYTES block per (peer, warp quad), peers in rank order
+    //   without the owner itself; a block holds OWN_CH chunks of 32 rows x 32 fp32 columns.
+    // Inside a 4 KB chunk, row r's 16-byte unit u sits at unit u ^ (r & 7): eight lanes (rows)
+    // touching the same unit hit eight different bank groups.
+    static constexpr int OWN_COLS = BN / SPLIT;
+    static constexpr int OWN_CH = OWN_COLS / 32;
+    static constexpr int SPLIT_CHUNK_BYTES = 32 * 32 * 4;
+    static constexpr int SLOT_BYTES = OWN_CH * SPLIT_CHUNK_BYTES;
+    static constexpr int RECV_BYTES = SPLIT > 1 ? (SPLIT - 1) * 4 * SLOT_BYTES : 0;
     static constexpr uint32_t SPLIT_TX_BYTES = static_cast<uint32_t>(RECV_BYTES);
     static_assert(SPLIT == 1 || SPLIT == 2 || SPLIT == 4, "split-K clusters of 2 or 4");
-    static_assert(SPLIT == 1 || (CTAS == 1 && !MX && KBS == 1), "split-K: single-CTA plain tiles");
-    static_assert(2 * RECV_BYTES <= STAGES * STAGE_BYTES, "receive and send blocks live in the stage ring");
-    static_assert(BN % 32 == 0 || SPLIT == 1, "split-K rows travel in 32-column chunks");
-    static_assert(SPLIT == 1 || (BN / 32 <= 8 && EPI_BUF_BYTES == 32 * 32 * 2), "split-K stores 32 x 32 chunks");
+    static_assert(SPLIT == 1 || (CTAS == 1 && !MX), "split-K: single-CTA plain tiles");
+    static_assert(SPLIT == 1 || BN % (32 * SPLIT) == 0, "split-K owners take whole 32-column chunks");
+    static_assert(RECV_BYTES <= STAGES * STAGE_BYTES, "the send staging lives in the stage ring");
+    static_assert(SPLIT == 1 || (OWN_CH <= 2 && EPI_BUF_BYTES == 32 * 32 * 2), "split-K stores 32 x 32 chunks");
     static_assert((TMEM_COLS & (TMEM_COLS - 1)) == 0, "tensor memory allocations are powers of two");
     static_assert(SMEM_BYTES <= 232448, "exceeds 227 KB of shared memory per CTA");
 };
@@ -369,8 +369,7 @@ __global__ void __launch_bounds__(192, 1)
     const uint32_t bar_tfull = bar_empty + STAGES * 8;
     const uint32_t bar_tempty = bar_tfull + 2 * 8;
     const uint32_t bar_drain = bar_tempty + 2 * 8;
-    const uint32_t bar_skfree = bar_drain + 8;   // split-K: peers' receive buffers free (SPLIT - 1 arrivals)
-    const uint32_t bar_skfull = bar_skfree + 8;  // split-K: this CTA's rows in from every peer (tx bytes)
+    const uint32_t bar_skfull = bar_drain + 8;  // split-K: this CTA's columns in from every peer (tx bytes)
     const uint32_t tmem_slot = base + S::OFF_MISC;
     volatile uint32_t* const tmem_slot_ptr = reinterpret_cast<volatile uint32_t*>(smem_gen + S::OFF_MISC);
     volatile uint32_t* const abort_flag = reinterpret_cast<volatile uint32_t*>(smem_gen + S::OFF_MISC + 4);
@@ -395,7 +394,6 @@ __global__ void __launch_bounds__(192, 1)
         }
         mbar_init(bar_drain, 1);
         if constexpr (SPLIT > 1) {
-            mbar_init(bar_skfree, SPLIT - 1);
             mbar_init(bar_skfull, 1);
         }
         *abort_flag = 0u;
@@ -724,161 +722,115 @@ __global__ void __launch_bounds__(192, 1)
 
             if constexpr (SPLIT > 1) {
                 // ---- split-K: this CTA holds K part `krank` of the whole 128 x BN tile ----
-                // 1. Its stage ring is idle (its MMAs are done): expect the peers' partials of the
-                //    rows it finishes, then tell every peer it may send them.
-                // 2. Once every peer's ring is idle, each warp whose rows another rank finishes
-                //    stages them (swizzled) and sends them with one bulk copy.
-                // 3. Once every peer's rows are in, all four warps fold the peers' partials into
-                //    one (rank order); the warps holding this rank's rows add their own partial
-                //    from tensor memory, scale, round and store.  The order is fixed, so the
-                //    result is the same on every call.
+                // 1. Every warp stages its 32 rows of each other rank's OWN_COLS columns (its stage
+                //    ring is idle: its MMAs are done) and sends them with one bulk copy per owner
+                //    into the owner's dedicated receive region, completing the owner's barrier.
+                //    No handshake: the region is never used for anything else.
+                // 2. Once every peer's columns are in, each warp adds the peers' partials (rank
+                //    order) and its own from tensor memory, scales, rounds and stores its 32 rows of
+                //    this rank's columns.  The order is fixed, so every call gives the same bits.
                 const uint32_t krank = cluster_ctarank();
-                if (epi_tid == 0) {
-                    // Expect the peers' bytes before any peer can learn that it may send them.
-                    mbar_arrive_expect_tx(bar_skfull, S::SPLIT_TX_BYTES);
-#pragma unroll
-                    for (uint32_t o = 0; o < static_cast<uint32_t>(SPLIT); ++o) {
-                        if (o != krank) mbar_arrive_cluster_release(mapa_shared(bar_skfree, o));
-                    }
-                }
-                bool ok = mbar_wait<true>(bar_skfree, 0, abort_flag, kErrSplitFree);
-                ok = named_bar_all(1, 128, __all_sync(0xffffffffu, ok));
-                if (!ok) break;
-                const uint32_t owner = quad / static_cast<uint32_t>(S::SPLIT_QUADS);
+                if (epi_tid == 0) mbar_arrive_expect_tx(bar_skfull, S::SPLIT_TX_BYTES);
                 const bool empty_part = w.kb_begin >= w.kb_end;  // fewer K blocks than ranks: zeros
-                constexpr int NC = BN / 32;
-                // Byte offset of row `lane`'s 16-byte unit u of chunk c inside a block.
-                auto swz = [&](int c, uint32_t u) {
-                    return static_cast<uint32_t>(c * 4096) + lane * 128u + (((u ^ lane) & 7u) << 4);
-                };
-                if (owner != krank) {
-                    // Stage chunk c while chunk c + 1 loads from tensor memory, then send it.
-                    const uint32_t first_own_quad = krank * S::SPLIT_QUADS;
-                    const uint32_t send_idx = quad < first_own_quad ? quad : quad - S::SPLIT_QUADS;
-                    const uint32_t stage_blk = base + S::OFF_A + S::RECV_BYTES + send_idx * S::WARP_BLOCK_BYTES;
-                    // This rank's slot among the owner's peers, and the warp's row group there.
-                    const uint32_t slot = krank < owner ? krank : krank - 1u;
-                    const uint32_t group = quad - owner * S::SPLIT_QUADS;
-                    const uint32_t dst_blk = mapa_shared(
-                        base + S::OFF_A + (slot * S::SPLIT_QUADS + group) * S::WARP_BLOCK_BYTES, owner);
-                    const uint32_t dst_bar = mapa_shared(bar_skfull, owner);
+                // Byte offset of row `lane`'s 16-byte unit u inside a 32 x 32 fp32 chunk.
+                auto swz = [&](uint32_t u) { return lane * 128u + (((u ^ lane) & 7u) << 4); };
+                const uint32_t stage_blk = base + S::OFF_A + epi_idx * ((SPLIT - 1) * S::SLOT_BYTES);
+                {
+                    // Items (owner, chunk) in order; tensor-memory loads run one item ahead.
+                    constexpr int NITEMS = (SPLIT - 1) * S::OWN_CH;
+                    auto item_col = [&](int it) {
+                        const uint32_t o_idx = static_cast<uint32_t>(it / S::OWN_CH);  // among the others
+                        const uint32_t owner = o_idx < krank ? o_idx : o_idx + 1u;
+                        return owner * S::OWN_COLS + static_cast<uint32_t>(it % S::OWN_CH) * 32u;
+                    };
                     uint32_t ra[32], rb[32];
-                    tmem_ld_32x32b_x32(tmem_row, ra);
+                    if (!empty_part) tmem_ld_32x32b_x32(tmem_row + item_col(0), ra);
 #pragma unroll
-                    for (int c = 0; c < NC; ++c) {
-                        uint32_t(&cur)[32] = (c & 1) ? rb : ra;
-                        uint32_t(&nxt)[32] = (c & 1) ? ra : rb;
-                        tmem_ld_wait(cur);
-                        if (c + 1 < NC) tmem_ld_32x32b_x32(tmem_row + (c + 1) * 32, nxt);
-#pragma unroll
-                        for (int j = 0; j < 8; ++j) {
-                            const uint32_t a = stage_blk + swz(c, static_cast<uint32_t>(j));
-                            if (empty_part) {
-                                st_shared_v4(a, 0u, 0u, 0u, 0u);
-                            } else {
-                                st_shared_v4(a, cur[4 * j], cur[4 * j + 1], cur[4 * j + 2], cur[4 * j + 3]);
-                            }
-                        }
-                    }
-                    fence_proxy_async_smem();  // the staged rows are visible to the bulk copy
-                    __syncwarp();
-                    if (lane == 0) bulk_copy_to_peer(dst_blk, stage_blk, S::WARP_BLOCK_BYTES, dst_bar);
-                }
-                ok = mbar_wait<true>(bar_skfull, 0, abort_flag, kErrSplitFull);
-                ok = named_bar_all(1, 128, __all_sync(0xffffffffu, ok));
-                if (!ok) break;
-                const uint32_t recv0 = base + S::OFF_A;
-                if constexpr (SPLIT > 2) {
-                    // All four warps fold the peers' partials (slots in rank order) into slot 0.
-#pragma unroll 1
-                    for (int item = static_cast<int>(epi_idx); item < S::SPLIT_QUADS * NC; item += 4) {
-                        const uint32_t g = static_cast<uint32_t>(item / NC);
-                        const int c = item % NC;
-                        float a[SPLIT - 1][32];
-#pragma unroll
-                        for (int s = 0; s < SPLIT - 1; ++s) {
-#pragma unroll
-                            for (int j = 0; j < 8; ++j) {
-                                ld_shared_v4f(recv0 + (s * S::SPLIT_QUADS + g) * S::WARP_BLOCK_BYTES +
-                                                  swz(c, static_cast<uint32_t>(j)),
-                                              a[s][4 * j], a[s][4 * j + 1], a[s][4 * j + 2], a[s][4 * j + 3]);
-                            }
-                        }
-#pragma unroll
-                        for (int s = 1; s < SPLIT - 1; ++s) {
-#pragma unroll
-                            for (int j = 0; j < 32; ++j) a[0][j] += a[s][j];
-                        }
-#pragma unroll
-                        for (int j = 0; j < 8; ++j) {
-                            st_shared_v4(recv0 + g * S::WARP_BLOCK_BYTES + swz(c, static_cast<uint32_t>(j)),
-                                         __float_as_uint(a[0][4 * j]), __float_as_uint(a[0][4 * j + 1]),
-                                         __float_as_uint(a[0][4 * j + 2]), __float_as_uint(a[0][4 * j + 3]));
-                        }
-                    }
-                    named_bar_sync(1, 128);
-                }
-                if (owner == krank) {
-                    // Peers' sum, then this rank's own partial from tensor memory: a fixed order.
-                    // The warps storing here share the eight epilogue staging buffers (no other
-                    // warp stores), so a chunk's store waits only for one NB chunks back.
-                    const uint32_t group = quad - owner * S::SPLIT_QUADS;
-                    const uint32_t sum_blk = recv0 + group * S::WARP_BLOCK_BYTES;
-                    const int out_row0 = mb * S::BM + static_cast<int>(quad) * 32;
-                    constexpr int NB = 8 / S::SPLIT_QUADS;
-                    const uint32_t buf0 = base + S::OFF_EPI + group * NB * S::EPI_BUF_BYTES;
-                    uint32_t ra[32], rb[32];
-                    tmem_ld_32x32b_x32(tmem_row, ra);
-#pragma unroll
-                    for (int c = 0; c < NC; ++c) {
-                        uint32_t(&cur)[32] = (c & 1) ? rb : ra;
-                        uint32_t(&nxt)[32] = (c & 1) ? ra : rb;
-                        tmem_ld_wait(cur);
-                        if (c + 1 < NC) tmem_ld_32x32b_x32(tmem_row + (c + 1) * 32, nxt);
-                        float v[32];
-#pragma unroll
-                        for (int j = 0; j < 8; ++j) {
-                            ld_shared_v4f(sum_blk + swz(c, static_cast<uint32_t>(j)), v[4 * j], v[4 * j + 1],
-                                          v[4 * j + 2], v[4 * j + 3]);
-                        }
+                    for (int it = 0; it < NITEMS; ++it) {
+                        uint32_t(&cur)[32] = (it & 1) ? rb : ra;
+                        uint32_t(&nxt)[32] = (it & 1) ? ra : rb;
                         if (!empty_part) {
+                            tmem_ld_wait(cur);
+                            if (it + 1 < NITEMS) tmem_ld_32x32b_x32(tmem_row + item_col(it + 1), nxt);
+                        }
+                        const uint32_t chunk = stage_blk + static_cast<uint32_t>(it) * S::SPLIT_CHUNK_BYTES;
 #pragma unroll
-                            for (int j = 0; j < 32; ++j) v[j] += __uint_as_float(cur[j]);
+                        for (int j = 0; j < 8; ++j) {
+                            if (empty_part) {
+                                st_shared_v4(chunk + swz(j), 0u, 0u, 0u, 0u);
+                            } else {
+                                st_shared_v4(chunk + swz(j), cur[4 * j], cur[4 * j + 1], cur[4 * j + 2], cur[4 * j + 3]);
+                            }
                         }
-                        // Scale, round and stage (64-byte swizzle: 16-byte group q of row `lane` at
-                        // q ^ ((lane / 2) % 4)); every NB chunks (or at the end) one fence, then
-                        // their TMA stores.
-                        const uint32_t buf = buf0 + static_cast<uint32_t>((c % NB) * S::EPI_BUF_BYTES);
-                        if (c >= NB && c % NB == 0) {
-                            if (lane == 0) bulk_wait_group_read<0>();  // the previous round's stores read
-                            __syncwarp();
-                        }
-#pragma unroll
-                        for (int q = 0; q < 4; ++q) {
-                            const uint32_t slot16 = static_cast<uint32_t>(q) ^ ((lane >> 1) & 3u);
-                            st_shared_v4(buf + lane * 64u + slot16 * 16u,
-                                         pack_bf16x2_rn(__fmul_rn(v[8 * q], s), __fmul_rn(v[8 * q + 1], s)),
-                                         pack_bf16x2_rn(__fmul_rn(v[8 * q + 2], s), __fmul_rn(v[8 * q + 3], s)),
-                                         pack_bf16x2_rn(__fmul_rn(v[8 * q + 4], s), __fmul_rn(v[8 * q + 5], s)),
-                                         pack_bf16x2_rn(__fmul_rn(v[8 * q + 6], s), __fmul_rn(v[8 * q + 7], s)));
-                        }
-                        if (c % NB == NB - 1 || c == NC - 1) {
-                            fence_proxy_async_smem();
+                        if (it % S::OWN_CH == S::OWN_CH - 1) {
+                            // All of this owner's chunks are staged: send them.
+                            fence_proxy_async_smem();  // the staged rows are visible to the bulk copy
                             __syncwarp();
                             if (lane == 0) {
-                                for (int cc = c - c % NB; cc <= c; ++cc) {
-                                    const int col0 = nb * BN + cc * 32;
-                                    const uint32_t src = buf0 + static_cast<uint32_t>((cc % NB) * S::EPI_BUF_BYTES);
-                                    if (out_row0 < p.M && col0 < p.N) {
-                                        tma_store_2d(&tm_c, col0, out_row0, src);
-                                        for (int i = 0; i < peers.count; ++i) {
-                                            tma_store_2d(&peers.maps[i], col0, out_row0, src);
-                                        }
-                                    }
-                                }
-                                bulk_commit_group();
+                                const uint32_t o_idx = static_cast<uint32_t>(it / S::OWN_CH);
+                                const uint32_t owner = o_idx < krank ? o_idx : o_idx + 1u;
+                                const uint32_t slot_at_owner = krank < owner ? krank : krank - 1u;
+                                const uint32_t src = stage_blk + o_idx * S::SLOT_BYTES;
+                                const uint32_t dst = mapa_shared(
+                                    base + S::OFF_RECV + (slot_at_owner * 4u + quad) * S::SLOT_BYTES, owner);
+                                bulk_copy_to_peer(dst, src, S::SLOT_BYTES, mapa_shared(bar_skfull, owner));
                             }
                         }
+                    }
+                }
+                bool ok = mbar_wait<true>(bar_skfull, 0, abort_flag, kErrSplitFull);
+                ok = named_bar_all(1, 128, __all_sync(0xffffffffu, ok));
+                if (!ok) break;
+                // This warp's rows of this rank's columns: peers' partials (rank order), then its own.
+                const int out_row0 = mb * S::BM + static_cast<int>(quad) * 32;
+                const uint32_t buf0 = base + S::OFF_EPI + epi_idx * 2u * S::EPI_BUF_BYTES;
+                uint32_t own[32];
+                if (!empty_part) tmem_ld_32x32b_x32(tmem_row + krank * S::OWN_COLS, own);
+#pragma unroll
+                for (int c = 0; c < S::OWN_CH; ++c) {
+                    float v[32];
+#pragma unroll
+                    for (int sl = 0; sl < SPLIT - 1; ++sl) {
+                        const uint32_t blk = base + S::OFF_RECV + (static_cast<uint32_t>(sl) * 4u + quad) * S::SLOT_BYTES +
+                                             static_cast<uint32_t>(c) * S::SPLIT_CHUNK_BYTES;
+#pragma unroll
+                        for (int j = 0; j < 8; ++j) {
+                            float x0, x1, x2, x3;
+                            ld_shared_v4f(blk + swz(j), x0, x1, x2, x3);
+                            if (sl == 0) {
+                                v[4 * j] = x0; v[4 * j + 1] = x1; v[4 * j + 2] = x2; v[4 * j + 3] = x3;
+                            } else {
+                                v[4 * j] += x0; v[4 * j + 1] += x1; v[4 * j + 2] += x2; v[4 * j + 3] += x3;
+                            }
+                        }
+                    }
+                    if (!empty_part) {
+                        tmem_ld_wait(own);
+#pragma unroll
+                        for (int j = 0; j < 32; ++j) v[j] += __uint_as_float(own[j]);
+                        if (c + 1 < S::OWN_CH) tmem_ld_32x32b_x32(tmem_row + krank * S::OWN_COLS + (c + 1) * 32, own);
+                    }
+                    // Scale, round and stage (64-byte swizzle: 16-byte group q of row `lane` at
+                    // q ^ ((lane / 2) % 4)) in this warp's staging buffer c, then store.
+                    const uint32_t buf = buf0 + static_cast<uint32_t>(c) * S::EPI_BUF_BYTES;
+#pragma unroll
+                    for (int q = 0; q < 4; ++q) {
+                        const uint32_t slot16 = static_cast<uint32_t>(q) ^ ((lane >> 1) & 3u);
+                        st_shared_v4(buf + lane * 64u + slot16 * 16u,
+                                     pack_bf16x2_rn(__fmul_rn(v[8 * q], s), __fmul_rn(v[8 * q + 1], s)),
+                                     pack_bf16x2_rn(__fmul_rn(v[8 * q + 2], s), __fmul_rn(v[8 * q + 3], s)),
+                                     pack_bf16x2_rn(__fmul_rn(v[8 * q + 4], s), __fmul_rn(v[8 * q + 5], s)),
+                                     pack_bf16x2_rn(__fmul_rn(v[8 * q + 6], s), __fmul_rn(v[8 * q + 7], s)));
+                    }
+                    fence_proxy_async_smem();
+                    __syncwarp();
+                    if (lane == 0) {
+                        const int col0 = nb * BN + static_cast<int>(krank) * S::OWN_COLS + c * 32;
+                        if (out_row0 < p.M && col0 < p.N) {
+                            tma_store_2d(&tm_c, col0, out_row0, buf);
+                            for (int i = 0; i < peers.count; ++i) tma_store_2d(&peers.maps[i], col0, out_row0, buf);
+                        }
+                        bulk_commit_group();
                     }
                 }
                 continue;

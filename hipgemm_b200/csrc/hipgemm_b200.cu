@@ -126,8 +126,8 @@ const KernelConfig kConfigs[] = {
     make_config<2, 256, 6>("pair256_s6", 1.0),
     make_config<2, 128, 8>("pair128_s8", 0.62),
     make_config<2, 224, 6>("pair224_s6", 0.90),
-    make_config<1, 128, 6, false, 1, 2>("bn128_s6_k2", 0.85),
-    make_config<1, 128, 6, false, 1, 4>("bn128_s6_k4", 0.70),
+    make_config<1, 128, 5, false, 1, 2>("bn128_s5_k2", 0.85),
+    make_config<1, 128, 5, false, 1, 4>("bn128_s5_k4", 0.70),
 };
 constexpr int kNumConfigs = sizeof(kConfigs) / sizeof(kConfigs[0]);
 
@@ -443,6 +443,42 @@ int check_args(const void* A, const void* B, void* C, int M, int N, int K, int c
     return HGEMM_OK;
 }
 
+// Per-thread cache of launch plans for the last few distinct calls without peer outputs: the
+// configuration, the schedule and the four tensor maps (A, B, and C with 32- and 128-row
+// boxes).  A hit skips the configuration choice and the tensor-map encodings, which are most of
+// the host time of a call (measured on B200: ~4 us per call before, with three maps).  A plan
+// depends only on the key's fields, so a buffer freed and reallocated at the same address with
+// the same shape may reuse it.
+struct PlanKey {
+    const void* a;
+    const void* b;
+    const void* c;
+    int M, N, K, ldc, config, schedule, dev;
+};
+struct PlanSlot {
+    PlanKey key;
+    bool valid;
+    int cfg;
+    Schedule sc;
+    CUtensorMap ta, tb, tc, tcw;
+};
+constexpr int kPlanCacheSlots = 16;
+thread_local PlanSlot t_plans[kPlanCacheSlots];
+
+bool same_key(const PlanKey& x, const PlanKey& y) {
+    return x.a == y.a && x.b == y.b && x.c == y.c && x.M == y.M && x.N == y.N && x.K == y.K && x.ldc == y.ldc &&
+           x.config == y.config && x.schedule == y.schedule && x.dev == y.dev;
+}
+
+PlanSlot& plan_slot(const PlanKey& k) {
+    uint64_t h = reinterpret_cast<uintptr_t>(k.a) ^ (reinterpret_cast<uintptr_t>(k.b) * 3) ^
+                 (reinterpret_cast<uintptr_t>(k.c) * 7);
+    h ^= (static_cast<uint64_t>(k.M) * 0x9E3779B1u) ^ (static_cast<uint64_t>(k.N) << 20) ^ static_cast<uint64_t>(k.K);
+    h ^= h >> 17;
+    h ^= h >> 9;
+    return t_plans[(h ^ (h >> 4)) % kPlanCacheSlots];
+}
+
 // workspace == nullptr: the library allocates it from its pool, stream-ordered.
 // peer_c[0..n_peer): more M x N outputs (same layout as C) that receive every C tile too.
 // ldc: C's row stride in elements (0: N), so that C can be a block of a wider matrix.
@@ -466,26 +502,53 @@ int run_gemm(const void* A, const void* B, void* C, int M, int N, int K, const f
         }
         return HGEMM_OK;
     }
-    const int c = config == 0 ? choose_config(M, N, K, *dev, schedule == HGEMM_SCHEDULE_AUTO) : config;
-    const KernelConfig& kc = kConfigs[c];
-    if (kc.kbs > 1 && K % 128 != 0) return HGEMM_ERR_UNSUPPORTED;  // (never chosen automatically then)
-    const Schedule sc = make_schedule(M, N, K, c, schedule, *dev);
-
-    const CUtensorMapSwizzle c_swizzle = kc.epi_cols == 64 ? CU_TENSOR_MAP_SWIZZLE_128B : CU_TENSOR_MAP_SWIZZLE_64B;
-    CUtensorMap ta, tb, tc;
-    if (!encode_operand(&ta, A, K, M, 128, kc.kbs) || !encode_operand(&tb, B, K, N, kc.b_box_rows, kc.kbs) ||
-        !encode_2d(&tc, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, C, static_cast<uint64_t>(N), static_cast<uint64_t>(M),
-                   static_cast<uint32_t>(kc.epi_cols), 32, c_swizzle, static_cast<uint64_t>(ldc) * 2)) {
-        return HGEMM_ERR_CUDA;
-    }
-    PeerOutputs peers{};
     if (n_peer < 0 || n_peer > kMaxPeerOutputs) return HGEMM_ERR_INVALID_VALUE;
-    // 128-row boxes for the CTA-wide stores of whole tiles (wide[0] = C).
-    if (!encode_2d(&peers.wide[0], CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, C, static_cast<uint64_t>(N),
-                   static_cast<uint64_t>(M), static_cast<uint32_t>(kc.epi_cols), 128, c_swizzle,
-                   static_cast<uint64_t>(ldc) * 2)) {
-        return HGEMM_ERR_CUDA;
+    const PlanKey key{A, B, C, M, N, K, ldc, config, schedule, static_cast<int>(dev - g_devices)};
+    PlanSlot* cached = nullptr;
+    if (n_peer == 0 && debug_stall == 0) {
+        PlanSlot& slot = plan_slot(key);
+        if (slot.valid && same_key(slot.key, key)) cached = &slot;
     }
+    int c = 0;
+    Schedule sc{};
+    CUtensorMap ta, tb, tc;
+    PeerOutputs peers{};
+    if (cached) {
+        c = cached->cfg;
+        sc = cached->sc;
+        ta = cached->ta;
+        tb = cached->tb;
+        tc = cached->tc;
+        peers.wide[0] = cached->tcw;
+    } else {
+        c = config == 0 ? choose_config(M, N, K, *dev, schedule == HGEMM_SCHEDULE_AUTO) : config;
+        const KernelConfig& kn = kConfigs[c];
+        if (kn.kbs > 1 && K % 128 != 0) return HGEMM_ERR_UNSUPPORTED;  // (never chosen automatically then)
+        sc = make_schedule(M, N, K, c, schedule, *dev);
+        const CUtensorMapSwizzle csw = kn.epi_cols == 64 ? CU_TENSOR_MAP_SWIZZLE_128B : CU_TENSOR_MAP_SWIZZLE_64B;
+        // C with 32-row boxes (per-warp stores) and 128-row boxes (CTA-wide stores of whole tiles).
+        if (!encode_operand(&ta, A, K, M, 128, kn.kbs) || !encode_operand(&tb, B, K, N, kn.b_box_rows, kn.kbs) ||
+            !encode_2d(&tc, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, C, static_cast<uint64_t>(N), static_cast<uint64_t>(M),
+                       static_cast<uint32_t>(kn.epi_cols), 32, csw, static_cast<uint64_t>(ldc) * 2) ||
+            !encode_2d(&peers.wide[0], CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, C, static_cast<uint64_t>(N),
+                       static_cast<uint64_t>(M), static_cast<uint32_t>(kn.epi_cols), 128, csw,
+                       static_cast<uint64_t>(ldc) * 2)) {
+            return HGEMM_ERR_CUDA;
+        }
+        if (n_peer == 0 && debug_stall == 0) {
+            PlanSlot& slot = plan_slot(key);
+            slot.key = key;
+            slot.cfg = c;
+            slot.sc = sc;
+            slot.ta = ta;
+            slot.tb = tb;
+            slot.tc = tc;
+            slot.tcw = peers.wide[0];
+            slot.valid = true;
+        }
+    }
+    const KernelConfig& kc = kConfigs[c];
+    const CUtensorMapSwizzle c_swizzle = kc.epi_cols == 64 ? CU_TENSOR_MAP_SWIZZLE_128B : CU_TENSOR_MAP_SWIZZLE_64B;
     for (int i = 0; i < n_peer; ++i) {
         if (!encode_2d(&peers.maps[i], CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, peer_c[i], static_cast<uint64_t>(N),
                        static_cast<uint64_t>(M), static_cast<uint32_t>(kc.epi_cols), 32, c_swizzle) ||

@@ -182,8 +182,8 @@ int hgemm_config_resident_ctas(int config);
 /* Synchronous.  Reads and clears the current device's kernel status word: 0 when no
  * bounded wait has expired since the last call, else the code of the first one,
  * role << 8 | site: 0x0101 producer (stage free), 0x0201 / 0x0202 / 0x0203 MMA issuer
- * (accumulator free, stage full, drain), 0x0301 epilogue (accumulator full), 0x0302 / 0x0303
- * split-K epilogue (peers' buffers free, peers' partial rows in). */
+ * (accumulator free, stage full, drain), 0x0301 epilogue (accumulator full), 0x0303
+ * split-K epilogue (peers' partial columns in). */
 int hgemm_device_status(uint32_t* status_out);
 
 /* Test hook: 1 if the library's stream-K workspace pool exists on `device` (it is created

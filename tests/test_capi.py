@@ -33,7 +33,7 @@ def test_library_metadata():
     L = hg.lib()
     assert L.hgemm_version().decode().startswith("hipgemm_b200")
     names = hg.config_names()
-    assert names[0] == "auto" and {"bn256_s4", "pair256_s6", "bn128_s6_k2", "bn128_s6_k4"} <= set(names)
+    assert names[0] == "auto" and {"bn256_s4", "pair256_s6", "bn128_s5_k2", "bn128_s5_k4"} <= set(names)
     assert L.hgemm_config_name(len(names)) is None
     for code in range(0, -7, -1):
         assert L.hgemm_error_string(code)

@@ -79,7 +79,7 @@ def test_every_tile_config(cuda_device, config, M, N, K):
     _run(M, N, K, config=config)
 
 
-@pytest.mark.parametrize("config", ["bn128_s6_k2", "bn128_s6_k4"])
+@pytest.mark.parametrize("config", ["bn128_s5_k2", "bn128_s5_k4"])
 @pytest.mark.parametrize("M,N,K", [(1, 8, 16), (7, 24, 48), (127, 136, 144), (129, 264, 272), (200, 520, 1040),
                                    (128, 8288, 8192), (256, 4104, 4112), (64, 2240, 16400)])
 def test_split_k_clusters(cuda_device, config, M, N, K):
@@ -106,7 +106,7 @@ def test_row_block_on_split_k(cuda_device):
     the rows outside the block are left untouched."""
     import hipgemm_b200 as hg
     M, N, K, r0, r1 = 384, 8192, 8192, 128, 256
-    assert hg.plan(r1 - r0, N, K)["config"] in {"bn128_s6_k2", "bn128_s6_k4"}
+    assert hg.plan(r1 - r0, N, K)["config"] in {"bn128_s5_k2", "bn128_s5_k4"}
     A, B, sa, sb = make_inputs(M, N, K, seed_a=5, seed_b=6)
     a, b, ta, tb = to_device(A, B, sa, sb)
     out = torch.full((M, N), 7.0, dtype=torch.bfloat16, device="cuda")
@@ -125,7 +125,7 @@ def test_split_k_chosen_for_skinny_shapes(cuda_device):
     """The automatic choice takes a split-K cluster configuration where the tiles of a
     128-row problem would leave most SMs idle, and not for large grids."""
     import hipgemm_b200 as hg
-    split = {"bn128_s6_k2", "bn128_s6_k4"}
+    split = {"bn128_s5_k2", "bn128_s5_k4"}
     assert hg.plan(128, 8192, 8192)["config"] in split
     assert hg.plan(8192, 8192, 8192)["config"] not in split
 
@@ -274,3 +274,27 @@ def test_from_host_pipeline_matches_device_path(cuda_device, M, N, K, pinned):
         torch.cuda.synchronize()
         assert torch.equal(hc.view(torch.int16), ref.cpu().view(torch.int16))
     assert hg.device_status() == 0
+
+
+def test_plan_cache_hits_and_evictions(cuda_device):
+    """The C ABI caches launch plans per (pointers, shape, config) in each host thread: calls
+    cycling over more distinct buffers than the cache holds (evictions), repeated (hits), and a
+    buffer reused with another shape all give the same bits as the first, uncached calls."""
+    import hipgemm_b200 as hg
+    M, N, K = 256, 384, 512
+    A, B, sa, sb = make_inputs(M, N, K, seed_a=11, seed_b=12)
+    a, b, ta, tb = to_device(A, B, sa, sb)
+    outs = [torch.empty((M, N), dtype=torch.bfloat16, device="cuda") for _ in range(24)]
+    first = [hg.fp8_gemm_tn(a, b, ta, tb, out=o).clone() for o in outs]
+    for _ in range(2):
+        for o, f in zip(outs, first):
+            o.zero_()
+            hg.fp8_gemm_tn(a, b, ta, tb, out=o)
+            assert torch.equal(o.view(torch.int16), f.view(torch.int16))
+    # Same C pointer, another shape (fewer rows of A): a different plan, correct result.
+    small = outs[0][: M // 2]
+    hg.fp8_gemm_tn(a[: M // 2], b, ta, tb, out=small)
+    torch.cuda.synchronize()
+    assert hg.device_status() == 0
+    assert torch.equal(small.view(torch.int16), first[0][: M // 2].view(torch.int16))
+    assert oracle.validate(c_bits(first[0]), oracle.gemm(A, B, sa, sb))[0] == 0

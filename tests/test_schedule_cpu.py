@@ -113,16 +113,16 @@ def _b200_resident():
     (cudaOccupancy*): 148 for every configuration except 4-CTA clusters (33 clusters fit)."""
     names = hg.config_names()
     res = (ctypes.c_int * len(names))(*([0] + [148] * (len(names) - 1)))
-    res[names.index("bn128_s6_k4")] = 132
+    res[names.index("bn128_s5_k4")] = 132
     return names, res
 
 
 @pytest.mark.parametrize("shape,auto,data_parallel", [
     ((8192, 8192, 8192), "pair256_s6", "pair256_s6"),        # the headline: 256 x 256 CTA-pair tiles
     ((16384, 28672, 8192), "pair256_s6", "pair256_s6"),
-    ((128, 8192, 8192), "bn128_s6_k2", "bn128_s6"),          # skinny, long K: split-K only under AUTO
-    ((64, 8192, 8192), "bn128_s6_k2", "bn128_s6"),
-    ((128, 4096, 8192), "bn128_s6_k4", "bn128_s6"),          # fewer tiles: four K parts
+    ((128, 8192, 8192), "bn128_s5_k2", "bn128_s6"),          # skinny, long K: split-K only under AUTO
+    ((64, 8192, 8192), "bn128_s5_k2", "bn128_s6"),
+    ((128, 4096, 8192), "bn128_s5_k4", "bn128_s6"),          # fewer tiles: four K parts
     ((128, 7168, 2048), "bn128_s6", "bn128_s6"),             # K too short for split-K to pay
     ((256, 8192, 8192), "bn128_s6", "bn128_s6"),             # 128 tiles: clusters would not fit at once
     ((1024, 8192, 8192), "pair224_s6", "pair224_s6"),        # the 8-GPU shard: two whole waves
@@ -141,9 +141,9 @@ def test_automatic_choice(shape, auto, data_parallel):
 def test_automatic_choice_respects_cluster_residency():
     """With fewer 4-CTA clusters resident than tiles, the four-way split gives way."""
     names, res = _b200_resident()
-    res[names.index("bn128_s6_k4")] = 120  # 30 clusters < 32 tiles of 128 x 4096
+    res[names.index("bn128_s5_k4")] = 120  # 30 clusters < 32 tiles of 128 x 4096
     L = hg.lib()
-    assert names[L.hgemm_debug_choose(128, 4096, 8192, hg.HGEMM_SCHEDULE_AUTO, res, len(names))] == "bn128_s6_k2"
+    assert names[L.hgemm_debug_choose(128, 4096, 8192, hg.HGEMM_SCHEDULE_AUTO, res, len(names))] == "bn128_s5_k2"
     assert L.hgemm_debug_choose(128, 4096, 8192, 0, res, len(names) - 1) == hg.HGEMM_ERR_INVALID_VALUE
     assert L.hgemm_debug_choose(0, 4096, 8192, 0, res, len(names)) == hg.HGEMM_ERR_INVALID_VALUE
     res[1] = 0

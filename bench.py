@@ -436,8 +436,9 @@ def parity_rows(M: int, world: int) -> list[int]:
 def parity_check(hg, sg, a_rows, b, sa, sb, c_rows, dev, world, rank, peer_bufs=None) -> dict:
     """Outside the timed region: this run's last result (c_rows, this rank's rows of
     a_rows . b^T) checked three ways.
-      1. rank 0: the rows of parity_rows() of the whole C against the CPU oracle
-         (oracle_gemm_row_list, the restated test.cpp:19-30) under |d| <= 1e-2|ref| + 1e-3;
+      1. rank 0: the rows of parity_rows() of the whole C as the ranks computed it (all-gathered
+         at N > 1) against the CPU oracle (oracle_gemm_row_list, the restated test.cpp:19-30)
+         under |d| <= 1e-2|ref| + 1e-3;
       2. N > 1, every rank: its block bit for bit against the same rows of a single-GPU call
          on the whole problem (A gathered from all ranks; whole-K kernels sum every element
          in the same order whatever the tiling);
@@ -471,14 +472,14 @@ def parity_check(hg, sg, a_rows, b, sa, sb, c_rows, dev, world, rank, peer_bufs=
         counts[1] = (c_rows.view(torch.int16) != single[sg.row_begin: sg.row_end].view(torch.int16)).sum()
         gathered = sg.all_gather(c_rows)
         counts[2] = (gathered.view(torch.int16) != single.view(torch.int16)).sum()
-        del gathered
         if peer_bufs is not None:
             peer_bufs.local.fill_(float("nan"))
             fused = run_allgather(sg, a_rows, b, peer_bufs, sa, sb)
             counts[3] = (fused.view(torch.int16) != single.view(torch.int16)).sum()
     rows = parity_rows(M, world)
     if rank == 0:
-        whole = single if single is not None else c_rows
+        # The sharded result itself: every rank's block, as gathered.
+        whole = gathered if world > 1 else c_rows
         got = whole[rows].view(torch.int16).cpu().numpy().view(np.uint16)
         A = a_full[rows].cpu().numpy()
         B = b.cpu().numpy()
@@ -498,6 +499,8 @@ def parity_check(hg, sg, a_rows, b, sa, sb, c_rows, dev, world, rank, peer_bufs=
             "block_mismatched": counts[1], "nccl_allgather_mismatched": counts[2],
             "fused_allgather_mismatched": counts[3] if peer_bufs is not None else None}
     del a_full, single
+    if world > 1:
+        del gathered
     return out
 
 

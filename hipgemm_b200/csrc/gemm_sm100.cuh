@@ -260,20 +260,14 @@ __device__ __forceinline__ void st_global_v4(float* p, float a, float b, float c
 // back), and the MX scale factors of both K blocks in one box each: half the TMA instructions
 // per K block, which matters because each costs the TMA unit a fixed time whatever its size.
 // SPLIT > 1: split-K over a cluster of SPLIT single CTAs (see the epilogue).
-template <int CTAS, int BN, int STAGES, bool MX = false, int KBS = 1, int SPLIT = 1, bool HM = false>
+template <int CTAS, int BN, int STAGES, bool MX = false, int KBS = 1, int SPLIT = 1>
 struct KernelShape {
-    // HM ("half M"): a CTA pair issuing M = 128 MMAs (cta_group::2), each CTA holding 64 rows of
-    // A and BN / 2 rows of B.  Its accumulator is a 64 x BN slice per CTA, laid out in tensor
-    // memory as two 64-lane halves: lanes [0, 64) hold columns [0, BN/2), lanes [64, 128)
-    // columns [BN/2, BN), each over BN/2 tensor-memory columns.  For problems of at most 128
-    // rows: twice the CTAs of 128-row tiles over the same columns, with no split of K.
-    static constexpr int ROWS = HM ? 64 : 128;  // rows of A and C per CTA
-    static constexpr int BM = ROWS * CTAS;   // output tile rows
+    static constexpr int BM = 128 * CTAS;   // output tile rows
     static constexpr int BK = 128;          // bytes of K per K block = one 128-byte swizzle row
     static constexpr int UMMA_K = 32;
     static constexpr int kNumThreads = 192;  // warp 0 TMA, warp 1 MMA, warps 2-5 epilogue
     static constexpr int B_ROWS = BN / CTAS;  // rows of B this CTA stages per K block
-    static constexpr int KB_A_BYTES = ROWS * BK;  // one K block of this CTA's A rows
+    static constexpr int KB_A_BYTES = 128 * BK;  // one K block of this CTA's A rows
     static constexpr int KB_B_BYTES = B_ROWS * BK;
     static constexpr int A_BYTES = KBS * KB_A_BYTES;  // per stage
     static constexpr int B_BYTES = KBS * KB_B_BYTES;
@@ -313,16 +307,13 @@ struct KernelShape {
     // block's factors (measured at 8192^3: 602 K cycles against 627 K with one set per K block
     // of the ring).
     static constexpr int SF_COLS = MX ? 4 * (1 + SFB_ATOMS) : 0;
-    static constexpr int ACC_COLS = HM ? BN / 2 : BN;  // tensor-memory columns per accumulator
-    static constexpr int OFF_SF_COL = ACC_BUFS * ACC_COLS;
-    static constexpr int COLS_USED = ACC_BUFS * ACC_COLS + SF_COLS;
+    static constexpr int OFF_SF_COL = ACC_BUFS * BN;
+    static constexpr int COLS_USED = ACC_BUFS * BN + SF_COLS;
     static constexpr uint32_t TMEM_COLS =
         COLS_USED <= 32 ? 32 : (COLS_USED <= 64 ? 64 : (COLS_USED <= 128 ? 128 : (COLS_USED <= 256 ? 256 : 512)));
     static constexpr uint32_t IDESC = idesc_e4m3_f32(BM, BN);
     static constexpr int PARTIAL_FLOATS = 128 * BN;  // one CTA's share of a partial tile
     static_assert(CTAS == 1 || CTAS == 2, "one CTA or a CTA pair");
-    static_assert(!HM || (CTAS == 2 && !MX && SPLIT == 1 && (BN / 2) % EPI_COLS == 0),
-                  "half-M: plain CTA pairs, whole epilogue chunks per half");
     static_assert(!MX || BN % 128 == 0, "MX tiles cover whole 128-row scale-factor atoms of B");
     static_assert(COLS_USED <= 512, "tensor memory holds 512 columns");
     static_assert(BN % 32 == 0 && BN >= 64 && BN <= 256, "BN must be a multiple of 32 in [64, 256]");
@@ -354,12 +345,12 @@ struct KernelShape {
 
 // KBS = 2 reads A and B through 3-D maps (x = 128 bytes of K, y = row, z = 128-byte K chunk);
 // KBS = 1 through 2-D maps (x = K byte, y = row).
-template <int CTAS, int BN, int STAGES, bool MX = false, int KBS = 1, int SPLIT = 1, bool HM = false>
+template <int CTAS, int BN, int STAGES, bool MX = false, int KBS = 1, int SPLIT = 1>
 __global__ void __launch_bounds__(192, 1)
     fp8_gemm_tn_sm100(const __grid_constant__ CUtensorMap tm_a, const __grid_constant__ CUtensorMap tm_b,
                       const __grid_constant__ CUtensorMap tm_c, const GemmParams p,
                       const __grid_constant__ PeerOutputs peers, const __grid_constant__ SfMaps sfm) {
-    using S = KernelShape<CTAS, BN, STAGES, MX, KBS, SPLIT, HM>;
+    using S = KernelShape<CTAS, BN, STAGES, MX, KBS, SPLIT>;
     extern __shared__ uint8_t smem_raw[];
     // 128-byte swizzle atoms need 1024-byte alignment.
     const uint32_t raw_base = smem_u32(smem_raw);
@@ -457,7 +448,7 @@ __global__ void __launch_bounds__(192, 1)
             for (int idx = 0; ok && have; ++idx, have = get_work(p, slot, nslots, idx, w)) {
                 int mb = mb_first, nb = nb_first;
                 if (idx > 0) tile_coords(w.tile, p, mb, nb);
-                const int a_row = mb * S::BM + static_cast<int>(rank) * S::ROWS;
+                const int a_row = mb * S::BM + static_cast<int>(rank) * 128;
                 const int b_row = nb * BN + static_cast<int>(rank) * S::B_ROWS;
                 for (int kb = w.kb_begin; kb < w.kb_end; kb += KBS) {
                     if (!mbar_wait<kPair>(bar_empty + 8 * stage, phase ^ 1u, abort_flag, kErrProducerEmpty)) {
@@ -545,7 +536,7 @@ __global__ void __launch_bounds__(192, 1)
                     break;
                 }
                 tc_fence_after();
-                const uint32_t d_tmem = tmem_base + static_cast<uint32_t>(acc * S::ACC_COLS);
+                const uint32_t d_tmem = tmem_base + static_cast<uint32_t>(acc * BN);
                 for (int kb = w.kb_begin; kb < w.kb_end; kb += KBS) {
                     if (!mbar_wait<kPair>(bar_full + 8 * stage, phase, abort_flag, kErrMmaFull)) {
                         ok = false;
@@ -726,12 +717,8 @@ __global__ void __launch_bounds__(192, 1)
             if (!ready) break;
             if (kPair && leader && epi_idx == 0 && lane == 0) mbar_arrive_cluster(peer_tfull0 + 8 * acc);
             tc_fence_after();
-            // Half-M: lane quadrants 0/1 hold rows 0-31/32-63 of the CTA's 64 rows in columns
-            // [0, BN/2), quadrants 2/3 the same rows in columns [BN/2, BN).
-            const int row0 = HM ? mb * S::BM + static_cast<int>(rank) * S::ROWS + static_cast<int>(quad & 1u) * 32
-                                : mb * S::BM + static_cast<int>(rank) * 128 + static_cast<int>(quad) * 32;
-            const int col_half = HM ? static_cast<int>(quad >> 1) * (BN / 2) : 0;
-            const uint32_t tmem_row = tmem_base + ((quad * 32u) << 16) + static_cast<uint32_t>(acc * S::ACC_COLS);
+            const int row0 = mb * S::BM + static_cast<int>(rank) * 128 + static_cast<int>(quad) * 32;
+            const uint32_t tmem_row = tmem_base + ((quad * 32u) << 16) + static_cast<uint32_t>(acc * BN);
 
             if constexpr (SPLIT > 1) {
                 // ---- split-K: this CTA holds K part `krank` of the whole 128 x BN tile ----
@@ -880,33 +867,6 @@ __global__ void __launch_bounds__(192, 1)
 #pragma unroll
                 for (int c = kDirect; c < BN / EC; ++c) {
                     store_packed(&held[(c - kDirect) * (EC / 2)], row0, nb * BN + c * EC);
-                }
-                continue;
-            }
-            if constexpr (HM) {
-                // Each warp stores its 32 rows of its half of the columns (per-warp stores: the
-                // CTA's two row halves are not one 128-row box).  Whole tiles only.
-                constexpr int NCH = (BN / 2) / EC;
-                uint32_t ra[EC], rb[EC];
-                auto load_half_chunk = [&](int c, uint32_t (&r)[EC]) {
-#pragma unroll
-                    for (int h = 0; h < EC / 32; ++h) {
-                        tmem_ld_32x32b_x32(tmem_row + c * EC + 32 * h, *reinterpret_cast<uint32_t(*)[32]>(&r[32 * h]));
-                    }
-                };
-                load_half_chunk(0, ra);
-#pragma unroll
-                for (int c = 0; c < NCH; ++c) {
-                    uint32_t(&cur)[EC] = (c & 1) ? rb : ra;
-                    uint32_t(&nxt)[EC] = (c & 1) ? ra : rb;
-                    tmem_ld_wait(*reinterpret_cast<uint32_t(*)[32]>(&cur[0]));
-                    if constexpr (EC == 64) reg_fence(*reinterpret_cast<uint32_t(*)[32]>(&cur[32]));
-                    if (c + 1 < NCH) {
-                        load_half_chunk(c + 1, nxt);
-                    } else {
-                        release_accumulator();
-                    }
-                    store_chunk(*reinterpret_cast<const float(*)[EC]>(&cur[0]), row0, nb * BN + col_half + c * EC);
                 }
                 continue;
             }

@@ -73,14 +73,12 @@ struct KernelConfig {
                   const PeerOutputs&, const SfMaps&, int grid, cudaStream_t);
     int kbs;    // K blocks per stage (2: 3-D operand maps, which need K % 128 == 0)
     int split;  // > 1: split-K over clusters of `split` CTAs, one tile per cluster
-    int a_box_rows;  // rows of A one CTA loads per K block (64 for half-M pairs, else 128)
-    bool hm;         // half-M pair: M = 128 MMAs over a CTA pair; whole tiles, M <= 128 only
 };
 
-template <int CTAS, int BN, int STAGES, bool MX = false, int KBS = 1, int SPLIT = 1, bool HM = false>
+template <int CTAS, int BN, int STAGES, bool MX = false, int KBS = 1, int SPLIT = 1>
 int launch_kernel(const CUtensorMap& ta, const CUtensorMap& tb, const CUtensorMap& tc, const GemmParams& p,
                   const PeerOutputs& peers, const SfMaps& sfm, int grid, cudaStream_t stream) {
-    using S = KernelShape<CTAS, BN, STAGES, MX, KBS, SPLIT, HM>;
+    using S = KernelShape<CTAS, BN, STAGES, MX, KBS, SPLIT>;
     cudaLaunchConfig_t cfg{};
     cfg.gridDim = dim3(static_cast<unsigned>(grid), 1, 1);
     cfg.blockDim = dim3(S::kNumThreads, 1, 1);
@@ -103,26 +101,25 @@ int launch_kernel(const CUtensorMap& ta, const CUtensorMap& tb, const CUtensorMa
     cfg.attrs = attr;
     cfg.numAttrs = n_attr;
     const cudaError_t e =
-        cudaLaunchKernelEx(&cfg, fp8_gemm_tn_sm100<CTAS, BN, STAGES, MX, KBS, SPLIT, HM>, ta, tb, tc, p, peers, sfm);
+        cudaLaunchKernelEx(&cfg, fp8_gemm_tn_sm100<CTAS, BN, STAGES, MX, KBS, SPLIT>, ta, tb, tc, p, peers, sfm);
     return e == cudaSuccess ? HGEMM_OK : HGEMM_ERR_CUDA;
 }
 
-template <int CTAS, int BN, int STAGES, bool MX = false, int KBS = 1, int SPLIT = 1, bool HM = false>
+template <int CTAS, int BN, int STAGES, bool MX = false, int KBS = 1, int SPLIT = 1>
 KernelConfig make_config(const char* name, double eff) {
-    using S = KernelShape<CTAS, BN, STAGES, MX, KBS, SPLIT, HM>;
+    using S = KernelShape<CTAS, BN, STAGES, MX, KBS, SPLIT>;
     return KernelConfig{name,         CTAS,
                         S::BM,        BN,
                         S::B_ROWS,    eff,
                         S::SMEM_BYTES, S::PARTIAL_FLOATS,
                         S::EPI_COLS,
-                        reinterpret_cast<const void*>(&fp8_gemm_tn_sm100<CTAS, BN, STAGES, MX, KBS, SPLIT, HM>),
-                        &launch_kernel<CTAS, BN, STAGES, MX, KBS, SPLIT, HM>,
-                        KBS,          SPLIT,
-                        S::ROWS,      HM};
+                        reinterpret_cast<const void*>(&fp8_gemm_tn_sm100<CTAS, BN, STAGES, MX, KBS, SPLIT>),
+                        &launch_kernel<CTAS, BN, STAGES, MX, KBS, SPLIT>,
+                        KBS,          SPLIT};
 }
 
 const KernelConfig kConfigs[] = {
-    {"auto", 0, 0, 0, 0, 0.0, 0, 0, 0, nullptr, nullptr, 0, 0, 0, false},
+    {"auto", 0, 0, 0, 0, 0.0, 0, 0, 0, nullptr, nullptr},
     make_config<1, 256, 4>("bn256_s4", 0.93),
     make_config<1, 128, 6>("bn128_s6", 0.70),
     make_config<1, 64, 8>("bn64_s8", 0.35),
@@ -131,8 +128,6 @@ const KernelConfig kConfigs[] = {
     make_config<2, 224, 6>("pair224_s6", 0.90),
     make_config<1, 128, 5, false, 1, 2>("bn128_s5_k2", 0.85),
     make_config<1, 128, 5, false, 1, 4>("bn128_s5_k4", 0.70),
-    make_config<2, 128, 12, false, 1, 1, true>("pairh128_s12", 0.90),
-    make_config<2, 128, 6, false, 2, 1, true>("pairh128_s6x2", 0.90),
 };
 constexpr int kNumConfigs = sizeof(kConfigs) / sizeof(kConfigs[0]);
 
@@ -415,7 +410,6 @@ int choose_config(int M, int N, int K, const int* resident_ctas, bool allow_spli
     for (int c = 1; c < kNumConfigs; ++c) {
         const KernelConfig& k = kConfigs[c];
         if (k.kbs > 1 && K % 128 != 0) continue;
-        if (k.hm) continue;  // half-M pairs only when asked for (measurements)
         const Schedule sc = make_schedule(M, N, K, c, HGEMM_SCHEDULE_DATA_PARALLEL, resident_ctas);
         // Split-K only where every cluster fits at once and each part keeps some depth.
         // (Measured on B200: with fewer than 16 K blocks per part the exchange and the
@@ -533,8 +527,7 @@ int run_gemm(const void* A, const void* B, void* C, int M, int N, int K, const f
         sc = make_schedule(M, N, K, c, schedule, *dev);
         const CUtensorMapSwizzle csw = kn.epi_cols == 64 ? CU_TENSOR_MAP_SWIZZLE_128B : CU_TENSOR_MAP_SWIZZLE_64B;
         // C with 32-row boxes (per-warp stores) and 128-row boxes (CTA-wide stores of whole tiles).
-        if (!encode_operand(&ta, A, K, M, kn.a_box_rows, kn.kbs) ||
-            !encode_operand(&tb, B, K, N, kn.b_box_rows, kn.kbs) ||
+        if (!encode_operand(&ta, A, K, M, 128, kn.kbs) || !encode_operand(&tb, B, K, N, kn.b_box_rows, kn.kbs) ||
             !encode_2d(&tc, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, C, static_cast<uint64_t>(N), static_cast<uint64_t>(M),
                        static_cast<uint32_t>(kn.epi_cols), 32, csw, static_cast<uint64_t>(ldc) * 2) ||
             !encode_2d(&peers.wide[0], CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, C, static_cast<uint64_t>(N),
@@ -555,7 +548,6 @@ int run_gemm(const void* A, const void* B, void* C, int M, int N, int K, const f
         }
     }
     const KernelConfig& kc = kConfigs[c];
-    if (kc.hm && sc.sk_tiles > 0) return HGEMM_ERR_UNSUPPORTED;  // half-M kernels store whole tiles only
     const CUtensorMapSwizzle c_swizzle = kc.epi_cols == 64 ? CU_TENSOR_MAP_SWIZZLE_128B : CU_TENSOR_MAP_SWIZZLE_64B;
     for (int i = 0; i < n_peer; ++i) {
         if (!encode_2d(&peers.maps[i], CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, peer_c[i], static_cast<uint64_t>(N),
@@ -623,7 +615,7 @@ int run_gemm_mx(const void* A, const void* B, void* C, int M, int N, int K, cons
     const int ci = config > 0 ? config - 1 : choose_mx_config(M, N, K, dev->mx_resident_ctas);
     const KernelConfig& kc = kMxConfigs[ci];
     CUtensorMap ta, tb, tc;
-    if (!encode_operand(&ta, A, K, M, kc.a_box_rows, kc.kbs) || !encode_operand(&tb, B, K, N, kc.b_box_rows, kc.kbs) ||
+    if (!encode_operand(&ta, A, K, M, 128, kc.kbs) || !encode_operand(&tb, B, K, N, kc.b_box_rows, kc.kbs) ||
         !encode_2d(&tc, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, C, static_cast<uint64_t>(N), static_cast<uint64_t>(M),
                    static_cast<uint32_t>(kc.epi_cols), 32,
                    kc.epi_cols == 64 ? CU_TENSOR_MAP_SWIZZLE_128B : CU_TENSOR_MAP_SWIZZLE_64B)) {

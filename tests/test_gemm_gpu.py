@@ -298,32 +298,3 @@ def test_plan_cache_hits_and_evictions(cuda_device):
     assert hg.device_status() == 0
     assert torch.equal(small.view(torch.int16), first[0][: M // 2].view(torch.int16))
     assert oracle.validate(c_bits(first[0]), oracle.gemm(A, B, sa, sb))[0] == 0
-
-
-@pytest.mark.parametrize("config", ["pairh128_s12", "pairh128_s6x2"])
-@pytest.mark.parametrize("M,N,K", [(128, 8192, 8192), (64, 2048, 4096), (1, 8, 128), (100, 1000, 1024),
-                                   (300, 520, 1024), (128, 136, 256)])
-def test_half_m_pairs(cuda_device, config, M, N, K):
-    """CTA pairs issuing M = 128 MMAs (64 rows of A per CTA, accumulator in two 64-lane halves):
-    every element matches the oracle, and the bits equal the single-CTA whole-K kernel's."""
-    import hipgemm_b200 as hg
-    names = hg.config_names()
-    A, B, sa, sb = make_inputs(M, N, K, seed_a=M + 3, seed_b=N + 5)
-    a, b, ta, tb = to_device(A, B, sa, sb)
-    out = hg.fp8_gemm_tn(a, b, ta, tb, config=names.index(config), schedule=hg.HGEMM_SCHEDULE_DATA_PARALLEL)
-    ref = hg.fp8_gemm_tn(a, b, ta, tb, config=names.index("bn128_s6"), schedule=hg.HGEMM_SCHEDULE_DATA_PARALLEL)
-    torch.cuda.synchronize()
-    assert hg.device_status() == 0
-    bad, n, first = check_against_oracle(c_bits(out), A, B, sa, sb)
-    assert bad == 0, f"{bad}/{n} mismatches (first {first}) at {M}x{N}x{K} {config}"
-    assert torch.equal(out.view(torch.int16), ref.view(torch.int16))
-
-
-def test_half_m_pairs_refuse_stream_k(cuda_device):
-    import hipgemm_b200 as hg
-    names = hg.config_names()
-    a = torch.zeros((1024, 1024), dtype=torch.uint8, device="cuda")
-    b = torch.zeros((1024, 1024), dtype=torch.uint8, device="cuda")
-    with pytest.raises(hg.HgemmError) as e:
-        hg.fp8_gemm_tn(a, b, config=names.index("pairh128_s12"), schedule=hg.HGEMM_SCHEDULE_STREAM_K)
-    assert e.value.code == hg.HGEMM_ERR_UNSUPPORTED

@@ -651,8 +651,9 @@ def run_ours(args) -> None:
         j = i % nbuf
         sg.run(A[j], B[j], SA[j], SB[j], out=C, config=config)
 
-    # NVML sampled every 0.1 ms: a 20-step headline run is only ~7 ms long.
-    sampler = ClockSampler(local_rank, period_s=0.0001)
+    # NVML sampled every 0.1 ms (a 20-step headline run is only ~7 ms long), on rank 0 only:
+    # with every rank sampling at once the NVML calls serialised and rank 0 got one sample.
+    sampler = ClockSampler(local_rank, period_s=0.0001) if rank == 0 else None
     ms, clocks = timed(gemm_step, args.steps, args.warmup, sampler)
     last_set = (args.warmup + args.steps - 1) % nbuf  # C holds this set's product now
     status = hg.device_status()

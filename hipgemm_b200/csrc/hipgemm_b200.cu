@@ -852,6 +852,59 @@ int hgemm_fp8_tn_rows_allgather(const void* A, const void* B, void* const* C_ran
                         reinterpret_cast<cudaStream_t>(stream), 0, HGEMM_SCHEDULE_DATA_PARALLEL, nullptr, 0, peers, n);
 }
 
+}  // extern "C"
+
+namespace hg {
+namespace {
+
+// Streams and events of the host-buffer pipeline, kept per host thread and device so that a
+// call does not create and destroy them (and two threads never share them).
+constexpr int kMaxPanels = 4;
+struct HostPipe {
+    bool ready = false;
+    cudaStream_t s_in = nullptr, s_mm = nullptr, s_out = nullptr;
+    cudaEvent_t ev_start = nullptr, ev_done = nullptr;
+    cudaEvent_t ev_in[2 * kMaxPanels] = {};  // one per arriving panel
+    cudaEvent_t ev_mm[2 * kMaxPanels] = {};  // one per rectangle computed
+};
+thread_local HostPipe t_pipes[kMaxDevices];
+
+HostPipe* host_pipe(int dev) {
+    HostPipe& hp = t_pipes[dev];
+    if (hp.ready) return &hp;
+    bool ok = cudaStreamCreateWithFlags(&hp.s_in, cudaStreamNonBlocking) == cudaSuccess &&
+              cudaStreamCreateWithFlags(&hp.s_mm, cudaStreamNonBlocking) == cudaSuccess &&
+              cudaStreamCreateWithFlags(&hp.s_out, cudaStreamNonBlocking) == cudaSuccess &&
+              cudaEventCreateWithFlags(&hp.ev_start, cudaEventDisableTiming) == cudaSuccess &&
+              cudaEventCreateWithFlags(&hp.ev_done, cudaEventDisableTiming) == cudaSuccess;
+    for (int i = 0; ok && i < 2 * kMaxPanels; ++i) {
+        ok = cudaEventCreateWithFlags(&hp.ev_in[i], cudaEventDisableTiming) == cudaSuccess &&
+             cudaEventCreateWithFlags(&hp.ev_mm[i], cudaEventDisableTiming) == cudaSuccess;
+    }
+    if (!ok) {
+        cudaGetLastError();
+        return nullptr;  // (partially created objects are kept for the next attempt's leak-free retry)
+    }
+    hp.ready = true;
+    return &hp;
+}
+
+// Panel boundaries of n rows: up to kMaxPanels panels of equal size in multiples of 256 rows
+// (whole pair tiles), at least 512 rows each.
+int split_panels(int n, int* bounds) {
+    const int want = std::max(1, std::min(kMaxPanels, n / 512));
+    const int step = ((n + want - 1) / want + 255) / 256 * 256;
+    int k = 0;
+    for (int b = 0; b < n; b += step) bounds[k++] = b;
+    bounds[k] = n;
+    return k;
+}
+
+}  // namespace
+}  // namespace hg
+
+extern "C" {
+
 int hgemm_fp8_tn_from_host(const void* A_host, const void* B_host, void* C_host, int M, int N, int K,
                            const float* h_scales, void* d_A, void* d_B, void* d_C, float* d_scales,
                            hgemm_stream_t stream) {
@@ -860,47 +913,34 @@ int hgemm_fp8_tn_from_host(const void* A_host, const void* B_host, void* C_host,
     if (M == 0 || N == 0) return HGEMM_OK;
     if (!C_host || (K > 0 && (!A_host || !B_host)) || (h_scales && !d_scales)) return HGEMM_ERR_INVALID_VALUE;
     int rc = HGEMM_OK;
-    if (!hg::current_device_setup(&rc)) return rc;
+    const hg::DeviceState* dev = hg::current_device_setup(&rc);
+    if (!dev) return rc;
+    hg::HostPipe* hp = hg::host_pipe(static_cast<int>(dev - hg::g_devices));
+    if (!hp) return HGEMM_ERR_CUDA;
     const cudaStream_t user = reinterpret_cast<cudaStream_t>(stream);
 
-    // Blocks: up to 4 x 4, rows and columns in multiples of 256 (whole pair tiles).  Finer
-    // blocks start the copy-back earlier but cost more in small GEMMs and copies: 8 x 8
-    // measured 4.1 ms against 3.7 ms for 8192^3 on a B200 over PCIe (2.9 ms is the time
-    // to move A + B in and C out with both directions busy).
-    constexpr int kMaxParts = 4;
-    auto split = [](int n, int parts[kMaxParts + 1]) {
-        const int want = n >= 4 * 512 ? 4 : (n >= 2 * 512 ? 2 : 1);
-        const int step = ((n + want - 1) / want + 255) / 256 * 256;
-        int k = 0;
-        for (int b = 0; b < n; b += step) parts[k++] = b;
-        parts[k] = n;
-        return k;
-    };
-    int rb[kMaxParts + 1], cb[kMaxParts + 1];
-    const int pm = split(M, rb), pn = split(N, cb);
-
-    cudaStream_t s_in = nullptr, s_mm = nullptr, s_out = nullptr;
-    cudaEvent_t ev_start = nullptr, ev_a[kMaxParts] = {}, ev_b[kMaxParts] = {}, ev_done = nullptr;
-    cudaEvent_t ev_c[kMaxParts * kMaxParts] = {};
+    // A arrives in row panels and B in column panels (rows of B), alternately, on one stream.
+    // Each arrival makes one new rectangle of C computable: a new A panel against every B panel
+    // already in, or a new B panel against every A panel already in.  That rectangle is one
+    // GEMM on a second stream and one 2-D copy back to C_host on a third, so both copy
+    // directions stay busy.  Measured at 8192^3 on B200 over PCIe: 4 panels per operand 3.67 ms,
+    // against 3.73 ms for 8 and 3.90 ms for 16 (more, smaller GEMMs and copies), and 3.73 ms
+    // for the earlier scheme of one GEMM per 2048 x 2048 block.
+    int rb[hg::kMaxPanels + 1], cb[hg::kMaxPanels + 1];
+    const int pm = hg::split_panels(M, rb), pn = hg::split_panels(N, cb);
     auto fail = [&](int code) {
         cudaGetLastError();
         return code;
     };
-    bool ok = cudaStreamCreateWithFlags(&s_in, cudaStreamNonBlocking) == cudaSuccess &&
-              cudaStreamCreateWithFlags(&s_mm, cudaStreamNonBlocking) == cudaSuccess &&
-              cudaStreamCreateWithFlags(&s_out, cudaStreamNonBlocking) == cudaSuccess &&
-              cudaEventCreateWithFlags(&ev_start, cudaEventDisableTiming) == cudaSuccess &&
-              cudaEventCreateWithFlags(&ev_done, cudaEventDisableTiming) == cudaSuccess;
-    for (int i = 0; ok && i < pm; ++i) ok = cudaEventCreateWithFlags(&ev_a[i], cudaEventDisableTiming) == cudaSuccess;
-    for (int j = 0; ok && j < pn; ++j) ok = cudaEventCreateWithFlags(&ev_b[j], cudaEventDisableTiming) == cudaSuccess;
-    for (int i = 0; ok && i < pm * pn; ++i) {
-        ok = cudaEventCreateWithFlags(&ev_c[i], cudaEventDisableTiming) == cudaSuccess;
-    }
 
     // Everything starts after the work already queued on the caller's stream.
-    ok = ok && cudaEventRecord(ev_start, user) == cudaSuccess && cudaStreamWaitEvent(s_in, ev_start, 0) == cudaSuccess &&
-         cudaStreamWaitEvent(s_mm, ev_start, 0) == cudaSuccess && cudaStreamWaitEvent(s_out, ev_start, 0) == cudaSuccess;
-    if (ok && h_scales) ok = cudaMemcpyAsync(d_scales, h_scales, 2 * sizeof(float), cudaMemcpyHostToDevice, s_in) == cudaSuccess;
+    bool ok = cudaEventRecord(hp->ev_start, user) == cudaSuccess &&
+              cudaStreamWaitEvent(hp->s_in, hp->ev_start, 0) == cudaSuccess &&
+              cudaStreamWaitEvent(hp->s_mm, hp->ev_start, 0) == cudaSuccess &&
+              cudaStreamWaitEvent(hp->s_out, hp->ev_start, 0) == cudaSuccess;
+    if (ok && h_scales) {
+        ok = cudaMemcpyAsync(d_scales, h_scales, 2 * sizeof(float), cudaMemcpyHostToDevice, hp->s_in) == cudaSuccess;
+    }
 
     const uint8_t* ha = static_cast<const uint8_t*>(A_host);
     const uint8_t* hb = static_cast<const uint8_t*>(B_host);
@@ -910,65 +950,44 @@ int hgemm_fp8_tn_from_host(const void* A_host, const void* B_host, void* C_host,
     uint8_t* hc = static_cast<uint8_t*>(C_host);
     const float* sa = h_scales ? d_scales : nullptr;
     const float* sb = h_scales ? d_scales + 1 : nullptr;
-
-    // Operand panels arrive alternately (A0, B0, A1, B1, ...); each C block is computed as
-    // soon as both of its panels are on the device and copied back as soon as it is done.
-    int na = 0, nbp = 0;
     const size_t ldc_bytes = static_cast<size_t>(N) * 2;
+
+    int na = 0, nbp = 0, arrival = 0;
     while (ok && (na < pm || nbp < pn)) {
         const bool take_a = na < pm && (na <= nbp || nbp >= pn);
-        if (take_a) {
-            const size_t off = static_cast<size_t>(rb[na]) * K, bytes = static_cast<size_t>(rb[na + 1] - rb[na]) * K;
-            if (bytes) ok = cudaMemcpyAsync(da + off, ha + off, bytes, cudaMemcpyHostToDevice, s_in) == cudaSuccess;
-            ok = ok && cudaEventRecord(ev_a[na], s_in) == cudaSuccess;
-            ++na;
-        } else {
-            const size_t off = static_cast<size_t>(cb[nbp]) * K, bytes = static_cast<size_t>(cb[nbp + 1] - cb[nbp]) * K;
-            if (bytes) ok = cudaMemcpyAsync(db + off, hb + off, bytes, cudaMemcpyHostToDevice, s_in) == cudaSuccess;
-            ok = ok && cudaEventRecord(ev_b[nbp], s_in) == cudaSuccess;
-            ++nbp;
+        const int* bounds = take_a ? rb : cb;
+        const int idx = take_a ? na : nbp;
+        const size_t off = static_cast<size_t>(bounds[idx]) * K;
+        const size_t bytes = static_cast<size_t>(bounds[idx + 1] - bounds[idx]) * K;
+        if (bytes) {
+            ok = cudaMemcpyAsync((take_a ? da : db) + off, (take_a ? ha : hb) + off, bytes, cudaMemcpyHostToDevice,
+                                 hp->s_in) == cudaSuccess;
         }
-        // Newly computable blocks: the new A panel with every B panel so far, or the
-        // new B panel with every A panel so far.
-        const int i_lo = take_a ? na - 1 : 0, i_hi = take_a ? na : na;
-        const int j_lo = take_a ? 0 : nbp - 1, j_hi = take_a ? nbp : nbp;
-        for (int i = i_lo; ok && i < i_hi; ++i) {
-            for (int j = j_lo; ok && j < j_hi; ++j) {
-                const int r0 = rb[i], r1 = rb[i + 1], c0 = cb[j], c1 = cb[j + 1];
-                ok = cudaStreamWaitEvent(s_mm, ev_a[i], 0) == cudaSuccess &&
-                     cudaStreamWaitEvent(s_mm, ev_b[j], 0) == cudaSuccess;
-                if (!ok) break;
-                rc = hg::run_gemm(da + static_cast<size_t>(r0) * K, db + static_cast<size_t>(c0) * K,
-                                  dc + static_cast<size_t>(r0) * ldc_bytes + static_cast<size_t>(c0) * 2, r1 - r0,
-                                  c1 - c0, K, sa, sb, s_mm, 0, HGEMM_SCHEDULE_DATA_PARALLEL, nullptr, 0, nullptr, 0,
-                                  N);
-                if (rc != HGEMM_OK) {
-                    ok = false;
-                    break;
-                }
-                cudaEvent_t e = ev_c[i * pn + j];
-                ok = cudaEventRecord(e, s_mm) == cudaSuccess && cudaStreamWaitEvent(s_out, e, 0) == cudaSuccess &&
-                     cudaMemcpy2DAsync(hc + static_cast<size_t>(r0) * ldc_bytes + static_cast<size_t>(c0) * 2,
-                                       ldc_bytes, dc + static_cast<size_t>(r0) * ldc_bytes + static_cast<size_t>(c0) * 2,
-                                       ldc_bytes, static_cast<size_t>(c1 - c0) * 2, static_cast<size_t>(r1 - r0),
-                                       cudaMemcpyDeviceToHost, s_out) == cudaSuccess;
-            }
+        ok = ok && cudaEventRecord(hp->ev_in[arrival], hp->s_in) == cudaSuccess &&
+             cudaStreamWaitEvent(hp->s_mm, hp->ev_in[arrival], 0) == cudaSuccess;
+        if (take_a) ++na; else ++nbp;
+        // The newly computable rectangle: rows [r0, r1) x columns [c0, c1).
+        const int r0 = take_a ? rb[na - 1] : 0, r1 = take_a ? rb[na] : rb[na];
+        const int c0 = take_a ? 0 : cb[nbp - 1], c1 = take_a ? cb[nbp] : cb[nbp];
+        if (ok && r1 > r0 && c1 > c0) {
+            rc = hg::run_gemm(da + static_cast<size_t>(r0) * K, db + static_cast<size_t>(c0) * K,
+                              dc + static_cast<size_t>(r0) * ldc_bytes + static_cast<size_t>(c0) * 2, r1 - r0, c1 - c0,
+                              K, sa, sb, hp->s_mm, 0, HGEMM_SCHEDULE_DATA_PARALLEL, nullptr, 0, nullptr, 0, N);
+            if (rc != HGEMM_OK) break;
+            cudaEvent_t e = hp->ev_mm[arrival];
+            ok = cudaEventRecord(e, hp->s_mm) == cudaSuccess && cudaStreamWaitEvent(hp->s_out, e, 0) == cudaSuccess &&
+                 cudaMemcpy2DAsync(hc + static_cast<size_t>(r0) * ldc_bytes + static_cast<size_t>(c0) * 2, ldc_bytes,
+                                   dc + static_cast<size_t>(r0) * ldc_bytes + static_cast<size_t>(c0) * 2, ldc_bytes,
+                                   static_cast<size_t>(c1 - c0) * 2, static_cast<size_t>(r1 - r0),
+                                   cudaMemcpyDeviceToHost, hp->s_out) == cudaSuccess;
         }
+        ++arrival;
     }
-    // The caller's stream resumes once every block is back on the host.
-    ok = ok && cudaEventRecord(ev_done, s_out) == cudaSuccess && cudaStreamWaitEvent(user, ev_done, 0) == cudaSuccess;
-
-    // Streams and events are released once their queued work completes.
-    for (cudaEvent_t e : ev_c) if (e) cudaEventDestroy(e);
-    for (int i = 0; i < kMaxParts; ++i) {
-        if (ev_a[i]) cudaEventDestroy(ev_a[i]);
-        if (ev_b[i]) cudaEventDestroy(ev_b[i]);
-    }
-    if (ev_start) cudaEventDestroy(ev_start);
-    if (ev_done) cudaEventDestroy(ev_done);
-    if (s_in) cudaStreamDestroy(s_in);
-    if (s_mm) cudaStreamDestroy(s_mm);
-    if (s_out) cudaStreamDestroy(s_out);
+    // The caller's stream resumes once every rectangle is back on the host.  The copy stream
+    // also orders after the GEMM stream (K == 0 or empty rectangles leave nothing to copy).
+    ok = ok && cudaEventRecord(hp->ev_done, hp->s_mm) == cudaSuccess &&
+         cudaStreamWaitEvent(hp->s_out, hp->ev_done, 0) == cudaSuccess &&
+         cudaEventRecord(hp->ev_done, hp->s_out) == cudaSuccess && cudaStreamWaitEvent(user, hp->ev_done, 0) == cudaSuccess;
     if (rc != HGEMM_OK) return fail(rc);
     return ok ? HGEMM_OK : fail(HGEMM_ERR_CUDA);
 }

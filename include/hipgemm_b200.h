@@ -62,11 +62,12 @@ int hgemm_fp8_tn_rows(const void* A, const void* B, void* C, int M, int N, int K
 
 /* The whole product from host buffers, as the reference's test.cpp:73-81 does it (copy A
  * and B in, launch, copy C out), pipelined: A and B go to the device in up to 4 row
- * panels each, alternately, on one internal stream; each of the up-to 4 x 4 C blocks is
- * computed on a second stream as soon as its A and B panels have arrived, and copied back
- * to C_host on a third as soon as it is done, so both copy directions and the GEMMs
- * overlap.  Host buffers should be pinned (cudaMallocHost) for the copies to be
- * asynchronous.  d_A (M x K), d_B (N x K), d_C (M x N bf16) and d_scales (2 floats) are
+ * panels each, alternately, on one internal stream; each arriving panel makes one rectangle
+ * of C computable (the new panel against every panel of the other operand already in),
+ * which is computed on a second stream and copied back to C_host on a third, so both copy
+ * directions and the GEMMs overlap.  The internal streams and events are created on a
+ * thread's first call on a device and kept for its later calls.  Host buffers should be
+ * pinned (cudaMallocHost) for the copies to be asynchronous.  d_A (M x K), d_B (N x K), d_C (M x N bf16) and d_scales (2 floats) are
  * caller-owned device buffers; h_scales (2 host floats: scale_a, scale_b) or NULL for 1.0.
  * Stream-ordered with respect to `stream` at both ends; host buffers must stay valid
  * until that stream reaches this point.  No counterpart in the reference. */

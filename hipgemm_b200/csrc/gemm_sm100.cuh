@@ -107,7 +107,8 @@ constexpr int kMaxPeerOutputs = 7;
 struct PeerOutputs {
     CUtensorMap maps[kMaxPeerOutputs];
     // The same outputs as C stores of 128-row boxes (one CTA's rows at once): wide[0] is this
-    // GPU's C, wide[1 + i] peer i's.  Whole data-parallel tiles are stored through these.
+    // GPU's C, wide[1 + i] peer i's (so wide[d] for destination d = 0 .. count).  Whole
+    // data-parallel tiles are stored through these.
     CUtensorMap wide[kMaxPeerOutputs + 1];
     int count;
 };
@@ -667,12 +668,16 @@ __global__ void __launch_bounds__(192, 1)
             fence_proxy_async_smem();
             if (lane == 0) bulk_wait_group_read<0>();  // this thread's last store has read its buffer
             named_bar_sync(2, 128);
-            if (lane == 0 && (wide_ctr & 3u) == epi_idx) {
-                if (cta_row0 < p.M && col0 < p.N) {
-                    tma_store_2d(&peers.wide[0], col0, cta_row0, buf);
-                    for (int i = 0; i < peers.count; ++i) tma_store_2d(&peers.wide[1 + i], col0, cta_row0, buf);
+            // Destination d (0 = this GPU's C, 1 + i = peer i's copy) goes out from warp
+            // (d + chunk) % 4: with peer outputs (the fused all-gather, up to 8 destinations) the
+            // four warps' lane 0s issue them in parallel.
+            if (lane == 0 && cta_row0 < p.M && col0 < p.N) {
+                bool issued = false;
+                for (int d = static_cast<int>((epi_idx - wide_ctr) & 3u); d <= peers.count; d += 4) {
+                    tma_store_2d(&peers.wide[d], col0, cta_row0, buf);
+                    issued = true;
                 }
-                bulk_commit_group();
+                if (issued) bulk_commit_group();
             }
             ++wide_ctr;
         };

@@ -79,7 +79,8 @@ int hgemm_fp8_tn_from_host(const void* A_host, const void* B_host, void* C_host,
  * C buffer as mapped into this process (C_ranks[rank] is this GPU's own; the others are
  * peer memory opened with hgemm_ipc_import, 1 <= nranks <= 8).  Rows [row_begin, row_end)
  * are computed here and every finished C tile is TMA-stored into all nranks buffers, so
- * the exchange over NVLink overlaps the math tile by tile.  When every rank's call has
+ * the exchange over NVLink overlaps the math tile by tile (the automatic choice takes a tile
+ * whose stores write 128-byte row segments, the efficient size across NVLink).  When every rank's call has
  * completed (order a barrier after it on the stream, e.g. a one-element NCCL all-reduce),
  * every buffer holds the whole C.  A caller that reuses the buffers must also put a
  * barrier between its last read of C and the next call.  No counterpart in the

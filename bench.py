@@ -17,8 +17,10 @@ NCCL all-gather and the fused GEMM + all-gather bit for bit against a single-GPU
 the whole problem ("parity" in the JSON line).  At N = 1 the line also carries the other
 benchmark configs ("configs"), each event-timed with cuBLASLt on the same buffers.
 
---impl reference times the reference's own CPU GEMM (test.cpp:19-30, restated in
-oracle/ because the reference needs ROCm + an MI355X) on this machine's host cores.
+--impl reference times the reference's own CPU GEMM (test.cpp:19-30) on this machine's
+host cores: its source compiled into oracle/_ref/libref_cpu.so with the ROCm element types
+restated (the GPU side needs ROCm and an MI355X), or where that library is absent the
+oracle's restatement of the loop nest.
 """
 from __future__ import annotations
 
@@ -241,10 +243,16 @@ class ClockSampler:
 
 def cpu_reference_rate(M: int, N: int, K: int, std_b: float, seed: int, budget_s: float, steps: int = 1,
                        warmup: int = 0) -> dict:
-    """Times the reference loop nest (OpenMP collapse(2), scalar fp32 accumulators) with
-    all host threads on a bounded sample of the workload: S rows x Ns columns x full K,
-    S chosen so each step takes about budget_s / (steps + warmup) seconds."""
+    """Times the reference's CPU GEMM with all host threads on a bounded sample of the
+    workload: S rows x Ns columns x full K, S chosen so each step takes about
+    budget_s / (steps + warmup) seconds.
+
+    The timed code is the reference's own gemm_cpu (test.cpp:19-30: OpenMP collapse(2),
+    scalar fp32 accumulators, unscaled) compiled from its sources into
+    oracle/_ref/libref_cpu.so (kind "reference"); where that library is absent, the oracle's
+    restatement of the same loop nest (kind "port")."""
     import oracle
+    from oracle import reference
     Ns = min(N, 2048)
     rows_avail = min(M, 4096)
     A, sa = oracle.make_quantized((rows_avail, K), seed)
@@ -252,8 +260,16 @@ def cpu_reference_rate(M: int, N: int, K: int, std_b: float, seed: int, budget_s
     # Every host core this process may run on, whatever OMP_NUM_THREADS says (torchrun
     # sets it to 1 per rank).
     threads = len(os.sched_getaffinity(0)) if hasattr(os, "sched_getaffinity") else (os.cpu_count() or 1)
+    if os.path.isfile(reference.LIB_PATH):
+        reference.set_num_threads(threads)
+        kind, what = "reference", "the reference's gemm_cpu (test.cpp:19-30) built from its sources, OpenMP"
+        run = lambda r0, r1: reference.gemm_cpu(A[r0:r1], B)
+    else:
+        kind, what = "port", "oracle_gemm_naive_rows (test.cpp:19-30 loop nest restated, OpenMP)"
+        run = lambda r0, r1: oracle.gemm_naive_rows(A, B, r0, r1, sa, sb, nthreads=threads)
+    run(0, 1)
     t0 = time.perf_counter()
-    oracle.gemm_naive_rows(A, B, 0, 1, sa, sb, nthreads=threads)
+    run(0, 1)
     t_row = max(time.perf_counter() - t0, 1e-6)
     per_step = budget_s / max(1, steps + warmup)
     S = int(max(1, min(rows_avail, per_step / t_row)))
@@ -261,15 +277,17 @@ def cpu_reference_rate(M: int, N: int, K: int, std_b: float, seed: int, budget_s
     for i in range(warmup + steps):
         r0 = (i * S) % max(1, rows_avail - S + 1)
         t0 = time.perf_counter()
-        oracle.gemm_naive_rows(A, B, r0, r0 + S, sa, sb, nthreads=threads)
+        run(r0, r0 + S)
         dt = time.perf_counter() - t0
         if i >= warmup:
             times.append(dt)
     mean = sum(times) / len(times)
     flops = 2.0 * S * Ns * K
-    return {"value": flops / mean / 1e12, "unit": "TFLOP/s", "cores": threads, "kind": "port",
+    if kind == "reference":
+        threads = reference.max_threads()
+    return {"value": flops / mean / 1e12, "unit": "TFLOP/s", "cores": threads, "kind": kind,
             "sample": f"{S} rows x {Ns} cols x K={K} of the {M}x{N}x{K} workload per step, "
-                      f"{steps} timed steps, oracle_gemm_naive_rows (test.cpp:19-30 loop nest, OpenMP)",
+                      f"{steps} timed steps, {what}",
             "ms_per_step": mean * 1e3}
 
 

@@ -1,10 +1,10 @@
 """ctypes binding of the CPU oracle (liboracle.so) — TEST INFRASTRUCTURE ONLY.
 
 Restates nirw4nna/hipgemm's CPU GEMM (test.cpp:19-30), validator (test.cpp:32-47) and
-input generator (utils.hpp:27-33); see oracle.h for what is and is not pinned
-("parity unpinned" at the reference level: the reference's CPU path needs ROCm
-headers that are absent here).  Only tests/, __graft_entry__.smoke() and bench.py's
-CPU-baseline legs may use it, and only as the checker or the timed CPU baseline.
+input generator (utils.hpp:27-33), pinned bit for bit to the reference's own copies of
+those functions compiled from its sources (oracle/reference.py; see oracle.h).  Only
+tests/, __graft_entry__.smoke() and bench.py's CPU-baseline legs may use it, and only as
+the checker or the timed CPU baseline.
 """
 from __future__ import annotations
 

@@ -1,8 +1,8 @@
 // CPU oracle for the FP8 e4m3 TN GEMM — TEST INFRASTRUCTURE ONLY (see oracle.h).
 //
 // Restates nirw4nna/hipgemm test.cpp:19-47 and utils.hpp:27-33 in portable C++.
-// Parity with the reference is unpinned: its CPU path needs ROCm headers that are
-// not on this machine.  Build with -ffp-contract=off and without -ffast-math so
+// Pinned bit for bit to the reference's own gemm_cpu, validate_matrix and init_random,
+// compiled from its sources (oracle/_ref, see oracle.h).  Build with -ffp-contract=off and without -ffast-math so
 // the k-sum keeps the reference's sequential fp32 order.
 #include "oracle.h"
 

@@ -7,11 +7,15 @@
  * CPU baseline of bench.py.  Nothing in the product (hipgemm_b200/, include/) may
  * link or call it: only tests/, __graft_entry__.smoke() and bench.py's CPU legs.
  *
- * PARITY UNPINNED (at the reference level).  The reference's CPU path cannot be
- * compiled here: gemm_cpu lives in test.cpp next to HIP code and needs ROCm
- * headers (hip_runtime.h, hip_fp8.h, hip_bfloat16.h) that this machine does not
- * have, and the reference ships no golden vectors or known-answer tests.  What is
- * pinned instead:
+ * PINNED to the reference's own CPU code.  gemm_cpu, validate_matrix (test.cpp:19-47)
+ * and init_random (utils.hpp:27-33) are compiled from the reference's files into
+ * oracle/_ref/libref_cpu.so (`make -C oracle ref`), with only the ROCm element types
+ * they use restated (ref_shim_types.h; the rest of those files is HIP code that g++
+ * cannot compile).  This library reproduces that one bit for bit, the reference's own
+ * test at its default 4096^3 included, and the fixtures it generated
+ * (tests/golden/reference/) carry the comparison to machines without the reference's
+ * sources (tests/test_oracle_reference.py).  The reference ships no golden vectors or
+ * known-answer tests of its own.  Also pinned:
  *   - the fp8 e4m3 codec against the OCP FP8 spec's table values and, bit for bit
  *     over every float in a sweep, against CUDA's host-callable
  *     __nv_cvt_float_to_fp8(x, __NV_SATFINITE, __NV_E4M3) (tests/test_oracle.py);

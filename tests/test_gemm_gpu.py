@@ -6,6 +6,8 @@ five benchmark configs (the column-blocked oracle, with every host core, takes s
 for 8192^3 and under a minute for the FFN shape), with the benchmark configs' tolerance
 |d| <= 1e-2*|ref| + 1e-3, distinct seeds and mixed-sign N(0,1) data.
 """
+import os
+
 import numpy as np
 import pytest
 import torch
@@ -53,8 +55,11 @@ def test_config4_ffn_full(cuda_device):
 
 def test_reference_parity_mode_4096(cuda_device):
     """test.cpp exactly: A and B both seed 0, N(-1, 1) cast straight to e4m3, no scale,
-    4096^3; the reference's own validator (signed 1% threshold) must pass too."""
+    4096^3; the reference's own validator (signed 1% threshold) must pass too.  Where the
+    reference's own CPU functions are built (oracle/_ref), C_ref is its gemm_cpu's output
+    and the verdict its validate_matrix's, as in test.cpp:76-85."""
     import hipgemm_b200 as hg
+    from oracle import reference
     A, B, _, _ = make_inputs(4096, 4096, 4096, seed_a=0, seed_b=0, mean_a=-1.0, mean_b=-1.0, scaled=False)
     assert np.array_equal(A, B)  # same seed, as in test.cpp:70-71
     a, b, _, _ = to_device(A, B, None, None)
@@ -63,6 +68,23 @@ def test_reference_parity_mode_4096(cuda_device):
     ref = oracle.gemm(A, B)
     assert oracle.validate(got, ref)[0] == 0
     assert oracle.validate_reference(got, ref)
+    if os.path.isfile(reference.LIB_PATH):
+        ref_own = reference.gemm_cpu(A, B)
+        assert np.array_equal(ref_own, ref)
+        assert reference.validate_matrix(got, ref_own)
+
+
+@pytest.mark.parametrize("case", ["test_cpp_256", "test_cpp_ragged", "bytes_ragged"])
+def test_reference_gemm_cpu_fixtures(cuda_device, case):
+    """The kernel (unit scales) against outputs of the reference's own gemm_cpu
+    (tests/golden/reference/gemm_cpu.npz), within |d| <= 1e-2*|ref| + 1e-3."""
+    import hipgemm_b200 as hg
+    g = np.load(os.path.join(os.path.dirname(os.path.abspath(__file__)), "golden", "reference", "gemm_cpu.npz"))
+    A, B, C_ref = g[f"{case}_A"], g[f"{case}_B"], g[f"{case}_C"]
+    a, b, _, _ = to_device(A, B, None, None)
+    got = c_bits(hg.fp8_gemm_tn(a, b))
+    bad, first = oracle.validate(got, C_ref)
+    assert bad == 0, f"{bad} mismatches against the reference's gemm_cpu (first flat index {first})"
 
 
 @pytest.mark.parametrize("M,N,K", [

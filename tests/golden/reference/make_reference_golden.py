@@ -10,8 +10,9 @@ the ROCm element types restated (oracle/ref_shim_types.h).  This script runs it 
                  both from init_random with its default seed 0, C = gemm_cpu(A, B);
   test_cpp_ragged the same generator (A seed 1, B seed 2) at 100 x 72 x 320, sizes that are
                  not multiples of any tile;
-  bytes_ragged   every finite e4m3 code (uniform bytes, NaN codes replaced), 37 x 29 x 384:
+  bytes_ragged   every finite e4m3 code (uniform bytes, NaN codes replaced), 37 x 40 x 384:
                  subnormals, +-448 and large products, which N(-1, 1) never reaches.
+(N is a multiple of 8 in all three: the library's C ABI needs 16-byte rows of C.)
 
 Each case stores A (M x K e4m3 bytes), B (N x K), C (M x N bf16 bits) and the reference
 validator's verdict on C against itself (`self_valid`: False when C holds a negative value,
@@ -40,7 +41,7 @@ def cases():
     for name, M, N, K, sa, sb in (("test_cpp_256", 256, 256, 256, 0, 0), ("test_cpp_ragged", 100, 72, 320, 1, 2)):
         out[name] = (ref.init_random(M * K, sa).reshape(M, K), ref.init_random(N * K, sb).reshape(N, K))
     A = rng.integers(0, 256, (37, 384), dtype=np.uint8)
-    B = rng.integers(0, 256, (29, 384), dtype=np.uint8)
+    B = rng.integers(0, 256, (40, 384), dtype=np.uint8)
     A[(A & 0x7F) == 0x7F] = 0x7E  # NaN codes -> 448
     B[(B & 0x7F) == 0x7F] = 0x01  # NaN codes -> the smallest subnormal
     out["bytes_ragged"] = (A, B)

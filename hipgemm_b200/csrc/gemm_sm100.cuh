@@ -881,14 +881,6 @@ __global__ void __launch_bounds__(192, 1)
                 // is in registers (before that chunk's store).
                 constexpr int NCH = BN / EC;
                 const int cta_row0 = mb * S::BM + static_cast<int>(rank) * 128;
-                // This CTA's last tile, with stores to this GPU alone: its MMAs have completed
-                // (the accumulator is full) and no copies remain, so the whole stage ring is
-                // idle.  Every chunk is staged in a ring slot of its own and the stores all go
-                // out after one barrier, without the double-buffered path's waits for buffer
-                // reuse: this epilogue is the one that nothing overlaps.
-                Work w_next;
-                const bool ring_last = !MX && SPLIT == 1 && peers.count == 0 && p.sk_tiles == 0 &&
-                                       !get_work(p, slot, nslots, idx + 1, w_next);
                 // With a stream-K schedule, partial tiles store through the per-warp buffers,
                 // which overlap the CTA-wide ones: every earlier store must have read its buffer
                 // before this tile stages into them.  (With peer outputs every store is per warp.)
@@ -921,18 +913,7 @@ __global__ void __launch_bounds__(192, 1)
                         packed[j] = pack_bf16x2_rn(__fmul_rn(__uint_as_float(cur[2 * j]), s),
                                                    __fmul_rn(__uint_as_float(cur[2 * j + 1]), s));
                     }
-                    if (ring_last) {
-                        static_assert(NCH * 4 * S::EPI_BUF_BYTES <= STAGES * S::STAGE_BYTES, "tile fits the ring");
-                        const uint32_t row_addr = base + S::OFF_A + static_cast<uint32_t>(c) * 4u * S::EPI_BUF_BYTES +
-                                                  quad * S::EPI_BUF_BYTES + lane * (EC * 2u);
-#pragma unroll
-                        for (int q = 0; q < EC / 8; ++q) {
-                            const uint32_t slot16 = EC == 64 ? (static_cast<uint32_t>(q) ^ (lane & 7u))
-                                                             : (static_cast<uint32_t>(q) ^ ((lane >> 1) & 3u));
-                            st_shared_v4(row_addr + slot16 * 16u, packed[4 * q], packed[4 * q + 1],
-                                         packed[4 * q + 2], packed[4 * q + 3]);
-                        }
-                    } else if (peers.count > 0) {
+                    if (peers.count > 0) {
                         // The fused all-gather stores per warp (32-row boxes, every warp's lane 0
                         // issuing its own stores to every destination), so that no chunk barrier
                         // couples the four warps to the slowest NVLink store.  (Measured at 8
@@ -942,21 +923,6 @@ __global__ void __launch_bounds__(192, 1)
                         store_packed(packed, row0, nb * BN + c * EC);
                     } else {
                         store_wide(packed, cta_row0, nb * BN + c * EC);
-                    }
-                }
-                if (ring_last) {
-                    fence_proxy_async_smem();
-                    named_bar_sync(2, 128);
-                    // Chunk c goes out from warp c % 4: each issuing thread has at most
-                    // ceil(NCH / 4) stores to issue.
-                    if (lane == 0 && cta_row0 < p.M) {
-                        for (int c = static_cast<int>(epi_idx); c < NCH; c += 4) {
-                            if (nb * BN + c * EC < p.N) {
-                                tma_store_2d(&peers.wide[0], nb * BN + c * EC, cta_row0,
-                                             base + S::OFF_A + static_cast<uint32_t>(c) * 4u * S::EPI_BUF_BYTES);
-                            }
-                        }
-                        bulk_commit_group();
                     }
                 }
                 if (p.sk_tiles > 0 && peers.count == 0) {

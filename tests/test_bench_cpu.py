@@ -56,3 +56,16 @@ def test_both_arms_report_the_same_config():
         c = bench.workload_config(name)
         M, N, K, _ = bench.WORKLOADS[name]
         assert (c["M"], c["N"], c["K"]) == (M, N, K) and "l2" in c
+
+
+def test_cpu_baseline_times_the_reference_function():
+    """The CPU baseline times the reference's own gemm_cpu where oracle/_ref holds it (kind
+    "reference"), else the oracle's restatement of the same loop (kind "port"), with every
+    host core, on a bounded sample."""
+    import os
+    from oracle import reference
+    r = bench.cpu_reference_rate(512, 512, 512, 1.0, 0, budget_s=0.5, steps=2, warmup=1)
+    expect = "reference" if os.path.isfile(reference.LIB_PATH) else "port"
+    assert r["kind"] == expect and r["unit"] == "TFLOP/s" and r["value"] > 0
+    assert r["cores"] == len(os.sched_getaffinity(0))
+    assert "512x512x512" in r["sample"]

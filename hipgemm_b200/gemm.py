@@ -30,8 +30,10 @@ def _stream_handle(stream: torch.cuda.Stream | None, device_index: int | None = 
     return torch.cuda.current_stream().cuda_stream or None
 
 
-# torch's raw current-stream query (a plain int); absent in some builds, then the public API.
+# torch's raw current-stream and current-device queries (plain ints); absent in some builds,
+# then the public API.
 _raw_stream = getattr(torch._C, "_cuda_getCurrentRawStream", None)
+_get_device = getattr(torch._C, "_cuda_getDevice", None)
 _fns: dict[str, object] = {}
 
 
@@ -76,6 +78,15 @@ def _check_scale(name: str, s: torch.Tensor | None, device: torch.device) -> Non
         raise ValueError(f"{name} must be a 1-element float32 tensor on {device}")
 
 
+def _scale_ptr(name: str, s: torch.Tensor | None, dev: int) -> int | None:
+    """The device pointer of a per-tensor scale on CUDA device `dev` (None = 1.0)."""
+    if s is None:
+        return None
+    if s.dtype != torch.float32 or s.numel() != 1 or s.get_device() != dev:
+        raise ValueError(f"{name} must be a 1-element float32 tensor on cuda:{dev}")
+    return s.data_ptr()
+
+
 def fp8_gemm_tn(a: torch.Tensor, b: torch.Tensor, scale_a: torch.Tensor | None = None,
                 scale_b: torch.Tensor | None = None, out: torch.Tensor | None = None, *, config: int = 0,
                 schedule: int = 0, workspace: torch.Tensor | None = None,
@@ -87,30 +98,39 @@ def fp8_gemm_tn(a: torch.Tensor, b: torch.Tensor, scale_a: torch.Tensor | None =
     not those of the whole-K kernels), 1 data-parallel only (whole-K tiles: the same bits for
     any tiling), 2 stream-K; workspace: optional caller-owned device buffer for a stream-K
     schedule (else the library's stream-ordered pool is used)."""
-    _check_operand("a", a)
-    _check_operand("b", b)
+    # The common case is checked with a few cheap integer and dtype tests (this wrapper's host
+    # time adds to every launch of a small GEMM); anything unusual takes the detailed checks,
+    # which raise the specific error.
+    dev = a.get_device()
+    if (dev < 0 or b.get_device() != dev or a.dtype not in _FP8_DTYPES or b.dtype not in _FP8_DTYPES
+            or a.dim() != 2 or b.dim() != 2 or not a.is_contiguous() or not b.is_contiguous()):
+        _check_operand("a", a)
+        _check_operand("b", b)
+        raise ValueError("a and b must be on the same device")
     M, K = a.shape
     N, Kb = b.shape
     if Kb != K:
         raise ValueError(f"K mismatch: a is {tuple(a.shape)}, b is {tuple(b.shape)}")
-    if b.device != a.device:
-        raise ValueError("a and b must be on the same device")
-    _check_scale("scale_a", scale_a, a.device)
-    _check_scale("scale_b", scale_b, a.device)
+    sa = _scale_ptr("scale_a", scale_a, dev)
+    sb = _scale_ptr("scale_b", scale_b, dev)
     if out is None:
         out = torch.empty((M, N), dtype=torch.bfloat16, device=a.device)
-    elif out.dtype != torch.bfloat16 or tuple(out.shape) != (M, N) or not out.is_contiguous():
+    elif (out.dtype != torch.bfloat16 or out.dim() != 2 or out.shape[0] != M or out.shape[1] != N
+          or not out.is_contiguous()):
         raise ValueError("out must be a contiguous (M, N) bfloat16 tensor")
     ws_ptr, ws_bytes = None, 0
     if workspace is not None:
-        if not workspace.is_cuda or workspace.device != a.device or not workspace.is_contiguous():
+        if workspace.get_device() != dev or not workspace.is_contiguous():
             raise ValueError("workspace must be a contiguous tensor on the operands' device")
         ws_ptr, ws_bytes = workspace.data_ptr(), workspace.numel() * workspace.element_size()
-    dev = a.device.index
-    with _on_device(dev):
-        rc = _fn("hgemm_fp8_tn_ex")(a.data_ptr(), b.data_ptr(), out.data_ptr(), M, N, K, _ptr(scale_a),
-                                    _ptr(scale_b), _stream_handle(stream, dev), int(config), int(schedule), ws_ptr,
-                                    ws_bytes)
+    f = _fns.get("hgemm_fp8_tn_ex") or _fn("hgemm_fp8_tn_ex")
+    if _get_device is not None and stream is None and _raw_stream is not None and _get_device() == dev:
+        rc = f(a.data_ptr(), b.data_ptr(), out.data_ptr(), M, N, K, sa, sb, _raw_stream(dev) or None,
+               int(config), int(schedule), ws_ptr, ws_bytes)
+    else:
+        with _on_device(dev):
+            rc = f(a.data_ptr(), b.data_ptr(), out.data_ptr(), M, N, K, sa, sb, _stream_handle(stream, dev),
+                   int(config), int(schedule), ws_ptr, ws_bytes)
     if rc:
         check(rc, "hgemm_fp8_tn")
     return out

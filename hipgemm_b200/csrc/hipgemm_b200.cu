@@ -6,6 +6,7 @@
 #include <cuda_runtime.h>
 
 #include <algorithm>
+#include <atomic>
 #include <cmath>
 #include <cstdio>
 #include <cstring>
@@ -35,8 +36,12 @@ constexpr int kGroupM = HG_GROUP_M;
 constexpr int kMaxConfigs = 16;
 
 struct DeviceState {
-    std::once_flag once;
-    int status = HGEMM_ERR_NO_DEVICE;
+    // Set-up runs under the mutex until it succeeds once; `ready` then makes every later call
+    // a single atomic load.  A failed set-up is not cached (a later call tries again), except
+    // a device this library was not built for, which stays refused.
+    std::mutex setup_mutex;
+    std::atomic<bool> ready{false};
+    bool wrong_arch = false;
     int num_sms = 0;
     // Persistent grid size per configuration: CTAs that can be resident at once.  For
     // CTA pairs this comes from cudaOccupancyMaxActiveClusters, which can be below
@@ -185,60 +190,59 @@ void init_encode() {
 int device_setup(int dev) {
     if (dev < 0 || dev >= kMaxDevices) return HGEMM_ERR_NO_DEVICE;
     DeviceState& st = g_devices[dev];
-    std::call_once(st.once, [&]() {
-        cudaDeviceProp prop{};
-        if (cudaGetDeviceProperties(&prop, dev) != cudaSuccess) return;
-        if (prop.major != 10) return;  // built for sm_100a only
-        std::call_once(g_encode_once, init_encode);
-        if (!g_encode) {
-            st.status = HGEMM_ERR_CUDA;
-            return;
+    if (st.ready.load(std::memory_order_acquire)) return HGEMM_OK;
+    std::lock_guard<std::mutex> lock(st.setup_mutex);
+    if (st.ready.load(std::memory_order_relaxed)) return HGEMM_OK;
+    if (st.wrong_arch) return HGEMM_ERR_NO_DEVICE;
+    cudaDeviceProp prop{};
+    if (cudaGetDeviceProperties(&prop, dev) != cudaSuccess) {
+        cudaGetLastError();
+        return HGEMM_ERR_NO_DEVICE;
+    }
+    if (prop.major != 10) {  // built for sm_100a only
+        st.wrong_arch = true;
+        return HGEMM_ERR_NO_DEVICE;
+    }
+    std::call_once(g_encode_once, init_encode);
+    if (!g_encode) return HGEMM_ERR_CUDA;
+    static_assert(kNumConfigs <= kMaxConfigs && kNumMxConfigs <= kMaxConfigs, "raise kMaxConfigs");
+    // Shared memory opt-in, then the CTAs that can be resident at once (0 on failure).
+    auto resident = [&](const KernelConfig& k) -> int {
+        if (cudaFuncSetAttribute(k.kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, k.smem_bytes) != cudaSuccess) {
+            cudaGetLastError();
+            return 0;
         }
-        static_assert(kNumConfigs <= kMaxConfigs && kNumMxConfigs <= kMaxConfigs, "raise kMaxConfigs");
-        // Shared memory opt-in, then the CTAs that can be resident at once (0 on failure).
-        auto resident = [&](const KernelConfig& k) -> int {
-            if (cudaFuncSetAttribute(k.kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, k.smem_bytes) !=
-                cudaSuccess) {
-                return 0;
-            }
-            const int csize = k.ctas * k.split;  // CTAs per cluster
-            if (csize == 1) return prop.multiProcessorCount;
-            cudaLaunchConfig_t cfg{};
-            cudaLaunchAttribute attr[1];
-            attr[0].id = cudaLaunchAttributeClusterDimension;
-            attr[0].val.clusterDim.x = csize;
-            attr[0].val.clusterDim.y = 1;
-            attr[0].val.clusterDim.z = 1;
-            cfg.gridDim = dim3(static_cast<unsigned>(csize * (prop.multiProcessorCount / csize)), 1, 1);
-            cfg.blockDim = dim3(192, 1, 1);
-            cfg.dynamicSmemBytes = static_cast<size_t>(k.smem_bytes);
-            cfg.attrs = attr;
-            cfg.numAttrs = 1;
-            int clusters = 0;
-            if (cudaOccupancyMaxActiveClusters(&clusters, k.kernel, &cfg) != cudaSuccess || clusters <= 0) {
-                cudaGetLastError();
-                return 0;
-            }
-            return clusters * csize;
-        };
-        for (int c = 1; c < kNumConfigs; ++c) {
-            st.resident_ctas[c] = resident(kConfigs[c]);
-            if (st.resident_ctas[c] == 0) {
-                st.status = HGEMM_ERR_CUDA;
-                return;
-            }
+        const int csize = k.ctas * k.split;  // CTAs per cluster
+        if (csize == 1) return prop.multiProcessorCount;
+        cudaLaunchConfig_t cfg{};
+        cudaLaunchAttribute attr[1];
+        attr[0].id = cudaLaunchAttributeClusterDimension;
+        attr[0].val.clusterDim.x = csize;
+        attr[0].val.clusterDim.y = 1;
+        attr[0].val.clusterDim.z = 1;
+        cfg.gridDim = dim3(static_cast<unsigned>(csize * (prop.multiProcessorCount / csize)), 1, 1);
+        cfg.blockDim = dim3(192, 1, 1);
+        cfg.dynamicSmemBytes = static_cast<size_t>(k.smem_bytes);
+        cfg.attrs = attr;
+        cfg.numAttrs = 1;
+        int clusters = 0;
+        if (cudaOccupancyMaxActiveClusters(&clusters, k.kernel, &cfg) != cudaSuccess || clusters <= 0) {
+            cudaGetLastError();
+            return 0;
         }
-        for (int c = 0; c < kNumMxConfigs; ++c) {
-            st.mx_resident_ctas[c] = resident(kMxConfigs[c]);
-            if (st.mx_resident_ctas[c] == 0) {
-                st.status = HGEMM_ERR_CUDA;
-                return;
-            }
-        }
-        st.num_sms = prop.multiProcessorCount;
-        st.status = HGEMM_OK;
-    });
-    return st.status;
+        return clusters * csize;
+    };
+    for (int c = 1; c < kNumConfigs; ++c) {
+        st.resident_ctas[c] = resident(kConfigs[c]);
+        if (st.resident_ctas[c] == 0) return HGEMM_ERR_CUDA;
+    }
+    for (int c = 0; c < kNumMxConfigs; ++c) {
+        st.mx_resident_ctas[c] = resident(kMxConfigs[c]);
+        if (st.mx_resident_ctas[c] == 0) return HGEMM_ERR_CUDA;
+    }
+    st.num_sms = prop.multiProcessorCount;
+    st.ready.store(true, std::memory_order_release);
+    return HGEMM_OK;
 }
 
 // The device's stream-K workspace pool, created on first use.  It keeps its memory (release

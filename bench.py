@@ -181,6 +181,11 @@ class ClockSampler:
                 idx = int(vis.split(",")[torch_device_index]) if vis else torch_device_index
                 self.h = pynvml.nvmlDeviceGetHandleByIndex(idx)
             self.max_mhz = int(pynvml.nvmlDeviceGetMaxClockInfo(self.h, pynvml.NVML_CLOCK_SM))
+            # One untimed query of each kind first: NVML's first reading of a device can take
+            # milliseconds, the whole of a short timed region (a 20-step run on 2 GPUs lasts
+            # ~4 ms and recorded one sample without this).
+            pynvml.nvmlDeviceGetClockInfo(self.h, pynvml.NVML_CLOCK_SM)
+            self._reasons()
         except Exception as e:  # no NVML: report it, do not guess
             self.error = f"nvml unavailable: {e}"
 

@@ -37,7 +37,9 @@ typedef struct CUstream_st* hgemm_stream_t;
 #define HGEMM_OK 0
 #define HGEMM_ERR_INVALID_VALUE (-1)   /* null pointer for a non-empty operand, negative size, bad range */
 #define HGEMM_ERR_ALIGNMENT (-2)       /* K % 16, N % 8, or a pointer not 16-byte aligned (TMA rules) */
-#define HGEMM_ERR_UNSUPPORTED (-3)     /* a size beyond what the kernels address (M, N, K < 2^31) */
+#define HGEMM_ERR_UNSUPPORTED (-3)     /* a valid request this entry point does not serve (a forced
+                                          two-K-block config with K % 128 != 0, a problem beyond a
+                                          fixed scratch or index range) */
 #define HGEMM_ERR_CUDA (-4)            /* a CUDA runtime/driver call failed (launch, tensor map, ...) */
 #define HGEMM_ERR_NO_DEVICE (-5)       /* no CUDA device, or not an sm_100 device */
 #define HGEMM_ERR_DEVICE_TIMEOUT (-6)  /* a bounded wait inside a kernel expired (see hgemm_device_status) */

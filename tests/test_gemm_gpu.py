@@ -306,7 +306,8 @@ def test_plan_cache_hits_and_evictions(cuda_device):
     M, N, K = 256, 384, 512
     A, B, sa, sb = make_inputs(M, N, K, seed_a=11, seed_b=12)
     a, b, ta, tb = to_device(A, B, sa, sb)
-    outs = [torch.empty((M, N), dtype=torch.bfloat16, device="cuda") for _ in range(24)]
+    # 40 distinct C buffers: more than the 32 plans a thread keeps, so the cycle evicts every time.
+    outs = [torch.empty((M, N), dtype=torch.bfloat16, device="cuda") for _ in range(40)]
     first = [hg.fp8_gemm_tn(a, b, ta, tb, out=o).clone() for o in outs]
     for _ in range(2):
         for o, f in zip(outs, first):

@@ -556,8 +556,14 @@ def config_legs(args, hg, dev, timed, peak, peak_sus, hbm_peak, skip: str) -> di
         # About 0.25 s of launches per leg (at least 20), estimated at 2 PFLOP/s.
         steps = int(max(20, min(2000, 0.25 / (flops / 2e15))))
         steps -= steps % nset
+        # Warm-up of a tenth of the timed launches (at least 5), the same for both arms: after a
+        # long GPU-bound leg the host needs some hundreds of calls to reach its steady call rate
+        # (measured on B200 boxes: ~11.5 us per Python call for the first few hundred calls of a
+        # process, ~6.5 us after), which a 5-launch warm-up left inside the timed region of the
+        # short launches.
+        warm = max(5, steps // 10)
         ms, _ = timed(lambda i: hg.fp8_gemm_tn(A[i % nset], B[i % nset], SA[i % nset], SB[i % nset], out=C),
-                      steps, 5)
+                      steps, warm)
         # The same launch sequence from a CUDA graph: no host time between launches.
         graph = torch.cuda.CUDAGraph()
         s = torch.cuda.Stream()
@@ -577,7 +583,7 @@ def config_legs(args, hg, dev, timed, peak, peak_sus, hbm_peak, skip: str) -> di
                 j = i % nset
                 torch._scaled_mm(A[j].view(torch.float8_e4m3fn), B[j].view(torch.float8_e4m3fn).t(),
                                  scale_a=SA[j], scale_b=SB[j], out_dtype=torch.bfloat16)
-            ms_lt, _ = timed(lt_step, steps, 5)
+            ms_lt, _ = timed(lt_step, steps, warm)
             lt = {"value": flops / (ms_lt * 1e-3) / 1e12, "unit": "TFLOP/s", "ms_per_launch": ms_lt}
         if hg.device_status() != 0:
             raise SystemExit(f"kernel status word set in the {name} leg: a bounded wait expired")
@@ -585,7 +591,7 @@ def config_legs(args, hg, dev, timed, peak, peak_sus, hbm_peak, skip: str) -> di
         pl = hg.plan(M, N, K)
         out[name] = {
             "workload": f"fp8_gemm_tn {M}x{N}x{K}", "tile_config": pl["config"],
-            "value": flops / (ms * 1e-3) / 1e12, "unit": "TFLOP/s", "ms_per_launch": ms, "launches": steps,
+            "value": flops / (ms * 1e-3) / 1e12, "unit": "TFLOP/s", "ms_per_launch": ms, "launches": steps, "warmup_launches": warm,
             "ms_per_launch_graph": ms_graph, "graph_tflops": flops / (ms_graph * 1e-3) / 1e12,
             "roofline": roofline(flops, alg, ms, peak, peak_sus, hbm_peak,
                                  TRAFFIC_BYTES_PER_LAUNCH.get((name, 1))),

@@ -556,12 +556,13 @@ def config_legs(args, hg, dev, timed, peak, peak_sus, hbm_peak, skip: str) -> di
         # About 0.25 s of launches per leg (at least 20), estimated at 2 PFLOP/s.
         steps = int(max(20, min(2000, 0.25 / (flops / 2e15))))
         steps -= steps % nset
-        # Warm-up of a tenth of the timed launches (at least 5), the same for both arms: after a
-        # long GPU-bound leg the host needs some hundreds of calls to reach its steady call rate
-        # (measured on B200 boxes: ~11.5 us per Python call for the first few hundred calls of a
-        # process, ~6.5 us after), which a 5-launch warm-up left inside the timed region of the
-        # short launches.
-        warm = max(5, steps // 10)
+        # Warm-up of half as many launches as are timed (at least 5), the same for both arms.
+        # The host takes a while to reach its steady call rate: measured on a B200 box, the
+        # Python call cost ~11.5 us for the first ~700 calls of a process and ~6.5 us after,
+        # and a 5-launch warm-up left the slow calls inside the timed region of the short
+        # launches (128 x 8192 x 8192: 22.2 us per launch back to back against 19.2 us from a
+        # CUDA graph on one box).
+        warm = max(5, steps // 2)
         ms, _ = timed(lambda i: hg.fp8_gemm_tn(A[i % nset], B[i % nset], SA[i % nset], SB[i % nset], out=C),
                       steps, warm)
         # The same launch sequence from a CUDA graph: no host time between launches.

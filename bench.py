@@ -556,13 +556,13 @@ def config_legs(args, hg, dev, timed, peak, peak_sus, hbm_peak, skip: str) -> di
         # About 0.25 s of launches per leg (at least 20), estimated at 2 PFLOP/s.
         steps = int(max(20, min(2000, 0.25 / (flops / 2e15))))
         steps -= steps % nset
-        # Warm-up of half as many launches as are timed (at least 5), the same for both arms.
-        # The host takes a while to reach its steady call rate: measured on a B200 box, the
-        # Python call cost ~11.5 us for the first ~700 calls of a process and ~6.5 us after,
-        # and a 5-launch warm-up left the slow calls inside the timed region of the short
-        # launches (128 x 8192 x 8192: 22.2 us per launch back to back against 19.2 us from a
-        # CUDA graph on one box).
-        warm = max(5, steps // 2)
+        # Untimed warm-up of at least half as many launches as are timed and about 50 ms of
+        # launches (at the same 2 PFLOP/s estimate), the same for both arms.  The host takes a
+        # while to reach its steady call rate: measured on B200 boxes, the Python call cost
+        # ~11.5 us for the first ~700 calls of a process and ~6.5 us after, and back-to-back
+        # 1024 x 7168 x 2048 launches took 21.9, 19.6 and 19.0 us in three consecutive 1000-launch
+        # loops; a 5-launch warm-up left that ramp inside the short legs' timed region.
+        warm = int(max(5, steps // 2, min(20000, 0.05 / (flops / 2e15))))
         ms, _ = timed(lambda i: hg.fp8_gemm_tn(A[i % nset], B[i % nset], SA[i % nset], SB[i % nset], out=C),
                       steps, warm)
         # The same launch sequence from a CUDA graph: no host time between launches.

@@ -3,6 +3,8 @@
 check against the oracle under |c - ref| <= 1e-2*|ref| + 1e-3."""
 from __future__ import annotations
 
+import hashlib
+
 import numpy as np
 import torch
 
@@ -23,9 +25,20 @@ def make_inputs(M: int, N: int, K: int, seed_a: int = 0, seed_b: int = 1, mean_a
     return A, B, sa, sb
 
 
+def sha256(buf) -> str:
+    """SHA-256 of a host array's or a device tensor's bytes (a device tensor is read back)."""
+    if isinstance(buf, torch.Tensor):
+        buf = buf.detach().contiguous().cpu().numpy()
+    return hashlib.sha256(np.ascontiguousarray(buf).tobytes()).hexdigest()
+
+
 def to_device(A: np.ndarray, B: np.ndarray, sa: float | None, sb: float | None, device="cuda:0"):
+    """A, B and the scales on the device.  The e4m3 bytes the GPU will read are read back and
+    hashed against the host buffers the oracle reads, so every parity test also proves that
+    both sides computed from bit-identical inputs."""
     a = torch.from_numpy(A).to(device)
     b = torch.from_numpy(B).to(device)
+    assert sha256(a) == sha256(A) and sha256(b) == sha256(B), "device operands differ from the oracle's bytes"
     ta = None if sa is None else torch.tensor([sa], dtype=torch.float32, device=device)
     tb = None if sb is None else torch.tensor([sb], dtype=torch.float32, device=device)
     return a, b, ta, tb

@@ -125,7 +125,9 @@ def _b200_resident():
     ((128, 4096, 8192), "bn128_s5_k4", "bn128_s6"),          # fewer tiles: four K parts
     ((128, 7168, 2048), "bn128_s6", "bn128_s6"),             # K too short for split-K to pay
     ((256, 8192, 8192), "bn128_s6", "bn128_s6"),             # 128 tiles: clusters would not fit at once
-    ((1024, 8192, 8192), "pair224_s6", "pair224_s6"),        # the 8-GPU shard: two whole waves
+    ((1024, 8192, 8192), "pair256_s6", "pair256_s6"),        # the 8-GPU shard: 2 waves either way
+    ((1024, 7168, 2048), "pair256_s6", "pair256_s6"),        # 2 waves either way: the wider tile
+    ((4000, 5120, 7168), "pair256_s6", "pair256_s6"),        # 5 waves either way
 ])
 def test_automatic_choice(shape, auto, data_parallel):
     """The configuration choice (host-only entry point, same code as the launch path) under the
@@ -148,3 +150,15 @@ def test_automatic_choice_respects_cluster_residency():
     assert L.hgemm_debug_choose(0, 4096, 8192, 0, res, len(names)) == hg.HGEMM_ERR_INVALID_VALUE
     res[1] = 0
     assert L.hgemm_debug_choose(128, 4096, 8192, 0, res, len(names)) == hg.HGEMM_ERR_INVALID_VALUE
+
+
+def test_automatic_choice_never_takes_the_224_wide_tile():
+    """Measured on B200, a 256x224 pair tile takes as long as a 256x256 one, and a narrower tile
+    never needs fewer waves: the automatic choice keeps the 224-wide tile for explicit requests."""
+    names, res = _b200_resident()
+    L = hg.lib()
+    for M in (256, 512, 1024, 2048, 4000, 4096, 8192):
+        for N in (1568, 4096, 5120, 7168, 8192, 9472, 28672):
+            for K in (2048, 8192):
+                for sched in (hg.HGEMM_SCHEDULE_AUTO, hg.HGEMM_SCHEDULE_DATA_PARALLEL):
+                    assert names[L.hgemm_debug_choose(M, N, K, sched, res, len(names))] != "pair224_s6", (M, N, K)

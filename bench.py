@@ -71,8 +71,8 @@ TRAFFIC_BYTES_PER_LAUNCH: dict[tuple[str, int], float] = {
     # profiles/fp8_gemm_tn_configs_dram_tensor.md:
     ("ffn", 1): 2109.891e6 + 923.742e6,            # <2, 256, 6> at 16384 x 28672 x 8192
     ("4096", 1): 33.639e6 + 2.364e6,               # <2, 256, 6> at 4096^3
-    ("1024x7168x2048", 1): 16.855e6 + 0.0,         # <2, 224, 6> (C still in L2 at kernel end)
-    ("4000x5120x7168", 1): 66.908e6 + 20.888e6,    # <2, 224, 6>
+    ("1024x7168x2048", 1): 16.855e6 + 0.0,         # <2, 256, 6> (C still in L2 at kernel end)
+    ("4000x5120x7168", 1): 67.779e6 + 19.442e6,    # <2, 256, 6>
 }
 
 

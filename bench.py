@@ -67,7 +67,9 @@ TRAFFIC_BYTES_PER_LAUNCH: dict[tuple[str, int], float] = {
     # ncu dram__bytes_read.sum + dram__bytes_write.sum of one launch of the automatic choice
     # (profiles/fp8_gemm_tn_8192_pair256.md, profiles/fp8_gemm_tn_128x8192x8192_splitk2.md):
     ("8192", 1): 232.149e6 + 117.133e6,    # fp8_gemm_tn_sm100<2, 256, 6> at 8192^3
-    ("skinny128", 1): 68.223e6 + 1.460e6,  # fp8_gemm_tn_sm100<1, 128, 6, 0, 1, 2> (split-K) at 128 x 8192 x 8192
+    # <1, 128, 6, 0, 1, 2> (split-K) at 128 x 8192 x 8192; the current <1, 128, 5, 0, 1, 2> loads the same
+    # tiles and exchanges partials in distributed shared memory, not DRAM:
+    ("skinny128", 1): 68.223e6 + 1.460e6,
     # profiles/fp8_gemm_tn_configs_dram_tensor.md:
     ("ffn", 1): 2109.891e6 + 923.742e6,            # <2, 256, 6> at 16384 x 28672 x 8192
     ("4096", 1): 33.639e6 + 2.364e6,               # <2, 256, 6> at 4096^3
